@@ -1,0 +1,146 @@
+/*
+ * nedo_gpu.h -- C ABI of the B200 (sm_100a) matvec library, libnedo_gpu.so.
+ *
+ * This is the boundary that replaces the CPU hot path of nedo.cpp:
+ *
+ *   void nedo::kernels::matvec(const TensorInfo& t, std::span<const std::byte> bytes,
+ *                              const float* x, float* y);                 kernels.hpp:20
+ *   void nedo::kernels::embedding_row(const TensorInfo& t, std::span<const std::byte> bytes,
+ *                                     uint32_t row, float* out);          kernels.hpp:21
+ *
+ * (paths relative to the nedo.cpp project: include/nedo/kernels.hpp,
+ * src/kernels.cpp:162-176).  The C++ forwarding layer in
+ * nedo.cpp_b200/cpp/nedo_kernels_cuda.cpp keeps those two signatures and calls
+ * the host-pointer entry points below, so src/model.cpp and src/pybind.cpp
+ * link unchanged.
+ *
+ * Conventions
+ *   - `type` is the GGUF tensor type code (include/nedo/gguf.hpp:18-19):
+ *     NEDO_GPU_F16 = 1, NEDO_GPU_Q4_0 = 2, NEDO_GPU_Q8_0 = 8.
+ *   - A weight is `rows` rows of `cols` elements, rows contiguous; `cols` is
+ *     the contiguous GGUF dimension (TensorInfo::shape[0]) and `rows` is
+ *     TensorInfo::shape[1].  Row size follows tensor_nbytes
+ *     (src/gguf.cpp:106-114): F16 2*cols, Q4_0 18*cols/32, Q8_0 34*cols/32.
+ *   - Activations and outputs are fp32.  Batched calls use x[batch][cols] and
+ *     y[batch][rows].
+ *   - Every function returns 0 on success or an NEDO_GPU_ERR_* code, never
+ *     throws, and leaves a message for nedo_gpu_last_error() (per thread).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Pointers named *_dev must be device memory on the current
+ *     CUDA device; *_host pointers are ordinary host memory.
+ */
+#ifndef NEDO_GPU_H
+#define NEDO_GPU_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NEDO_GPU_API __attribute__((visibility("default")))
+#else
+#define NEDO_GPU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    NEDO_GPU_F16 = 1,
+    NEDO_GPU_Q4_0 = 2,
+    NEDO_GPU_Q8_0 = 8
+};
+
+enum {
+    NEDO_GPU_OK = 0,
+    NEDO_GPU_ERR_TYPE = 1,    /* type not supported by this entry point          */
+    NEDO_GPU_ERR_ALIGN = 2,   /* Q4_0/Q8_0 column count not a multiple of 32      */
+    NEDO_GPU_ERR_ROW = 3,     /* embedding row out of range                        */
+    NEDO_GPU_ERR_ARG = 4,     /* null pointer, size mismatch, unsupported size     */
+    NEDO_GPU_ERR_CUDA = 5,    /* CUDA runtime error (message names the call)       */
+    NEDO_GPU_ERR_DEVICE = 6,  /* a kernel gave up on a bounded wait                */
+    NEDO_GPU_ERR_NOMEM = 7    /* device or pinned allocation failed                */
+};
+
+/* Library version: major*10000 + minor*100 + patch. */
+NEDO_GPU_API int nedo_gpu_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+NEDO_GPU_API const char* nedo_gpu_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Host-pointer entry points: drop-in semantics of the reference.
+ *
+ * Synchronous: the result is in y_host/out_host on return, like the CPU
+ * kernel.  The weight bytes are uploaded to the device on first use and kept
+ * resident, keyed by (w_host, w_bytes) -- the reference passes spans into a
+ * GGUF mmap that stay valid and unchanged for the model's lifetime
+ * (src/gguf.cpp:139).  A caller that rewrites a weight buffer in place must
+ * call nedo_gpu_weight_evict() first.  Calls are serialised per device.
+ * ------------------------------------------------------------------------- */
+
+/* Replaces nedo::kernels::matvec (src/kernels.cpp:162-169):
+ *   y_host[r] = sum_i dequant(w)[r][i] * x_host[i], r < rows.
+ * Errors mirror the reference: a Q4_0/Q8_0 column count that is not a
+ * multiple of 32 ("... elements not block aligned", src/gguf.cpp:109-110),
+ * an unsupported type ("matvec tensor type not supported", src/kernels.cpp:168).
+ * w_bytes must be at least rows * row_bytes. */
+NEDO_GPU_API int nedo_gpu_matvec(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                    const float* x_host, float* y_host);
+
+/* Replaces nedo::kernels::embedding_row (src/kernels.cpp:170-176): writes the
+ * dequantised row `row` (cols floats) to out_host, bit-identical to the
+ * reference.  row >= rows -> NEDO_GPU_ERR_ROW ("bad embedding row"). */
+NEDO_GPU_API int nedo_gpu_embedding_row(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                           uint32_t row, float* out_host);
+
+/* Upload (or find) the resident device copy of a host weight buffer.
+ * *w_dev_out receives the device pointer (valid until evicted). */
+NEDO_GPU_API int nedo_gpu_weight_upload(const void* w_host, uint64_t w_bytes, const void** w_dev_out);
+/* Drop the resident copy of w_host (no-op if absent). */
+NEDO_GPU_API int nedo_gpu_weight_evict(const void* w_host);
+/* Drop every resident weight on every device this library touched. */
+NEDO_GPU_API int nedo_gpu_cache_clear(void);
+
+/* ---------------------------------------------------------------------------
+ * Device-pointer entry points (asynchronous on `stream`).
+ * ------------------------------------------------------------------------- */
+
+/* The matvec of nedo_gpu_matvec on device buffers, for `batch` activation
+ * vectors: y_dev[b][r] = dot(row r, x_dev[b]), b < batch.  batch == 1 is the
+ * decode path (src/model.cpp:217-259); batch > 1 replaces `batch` serial
+ * calls over the same weight, which is how the reference processes a prompt
+ * (src/model.cpp:262-266). */
+NEDO_GPU_API int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
+                        float* y_dev, uint32_t batch, void* stream);
+
+/* matvec followed by the greedy pick of the LM head (std::max_element over
+ * the logits, src/model.cpp:36: first index of the maximum), fused into the
+ * matvec kernel where the shape allows.  y_dev receives the logits;
+ * index_dev (int64) the argmax; value_dev (may be NULL) its value.  Uses a
+ * per-device scratch area: calls that overlap on the GPU must not share a
+ * device. */
+NEDO_GPU_API int nedo_gpu_matvec_argmax_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
+                               float* y_dev, int64_t* index_dev, float* value_dev, void* stream);
+
+/* argmax of an fp32 vector in device memory (first index of the maximum). */
+NEDO_GPU_API int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev, void* stream);
+
+/* embedding_row for rows [row_begin, row_begin + row_count) into
+ * out_dev[row_count][cols]; bit-identical to the reference. */
+NEDO_GPU_API int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, uint64_t row_begin,
+                              uint64_t row_count, float* out_dev, void* stream);
+
+/* Wait for `stream`, then report (and clear) device-side failures recorded
+ * by kernels on the current device since the last check. */
+NEDO_GPU_API int nedo_gpu_status(void* stream);
+
+/* Describe the kernel choice for a shape: out[0] = path (1 streaming,
+ * 2 generic, 3 batched tensor-core), out[1] grid, out[2] threads,
+ * out[3] dynamic shared bytes, out[4] rows per tile, out[5] stages,
+ * out[6] chunks, out[7] groups.  n = capacity of out (>= 8). */
+NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEDO_GPU_H */

@@ -1,0 +1,16 @@
+// Declaration-compatible subset of nedo.cpp's include/nedo/kernels.hpp: the two
+// hot-path entry points (kernels.hpp:20-21) and the fp16 helpers the kernel
+// tests use (kernels.hpp:9-10).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <span>
+
+#include "nedo/gguf.hpp"
+
+namespace nedo::kernels {
+float fp16_to_fp32(uint16_t h) noexcept;
+uint16_t fp32_to_fp16(float f) noexcept;
+void matvec(const TensorInfo& t, std::span<const std::byte> bytes, const float* x, float* y);
+void embedding_row(const TensorInfo& t, std::span<const std::byte> bytes, uint32_t row, float* out);
+}  // namespace nedo::kernels

@@ -1,0 +1,58 @@
+// launch.h -- host-side launchers of the matvec kernels (internal to libnedo_gpu.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace nedo_gpu {
+
+// Argmax bookkeeping for the fused LM-head path: one candidate per CTA plus a
+// self-resetting completion counter (the last CTA to finish folds the
+// candidates and writes the winner).
+struct ArgmaxScratch {
+    float* cand_val;      // [max_ctas]
+    uint32_t* cand_idx;   // [max_ctas] (row index of the candidate)
+    uint32_t* counter;    // starts at 0, reset to 0 by the last CTA
+    int64_t* out_index;   // result
+    float* out_value;     // result (may be null)
+};
+
+struct StreamPlan {
+    bool ok = false;
+    uint32_t chunks = 0;         // warps that split one row's columns
+    uint32_t groups = 0;         // independent row groups per CTA
+    uint32_t rows_per_tile = 0;  // rows moved by one bulk copy
+    uint32_t stages = 0;         // ring depth
+    uint32_t stage_bytes = 0;
+    uint32_t threads = 0;
+    uint32_t smem_bytes = 0;
+    uint32_t grid = 0;
+    uint64_t tiles = 0;
+};
+
+StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin);
+
+// Batch-1 streaming GEMV over GGUF bytes.  w/x/y are device pointers on the
+// current device.  When `amax` is non-null (F16 only) the argmax of y is also
+// produced, first index on ties.
+cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, const float* x, float* y,
+                          uint64_t rows, uint64_t cols, DeviceStatus* status, const ArgmaxScratch* amax,
+                          cudaStream_t stream);
+
+// Any shape the streaming kernel does not take (odd row sizes, unaligned
+// pointers): one warp per row, byte-granular loads.  x is [batch][ldx], y [batch][ldy].
+cudaError_t launch_generic(uint32_t type, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
+                           uint32_t batch, uint64_t ldx, uint64_t ldy, cudaStream_t stream);
+
+// embedding_row: out[i] = d * q[i] for one row (bit-exact with the reference).
+cudaError_t launch_dequant_rows(uint32_t type, const void* w, uint64_t rows, uint64_t cols, uint64_t row_begin,
+                                uint64_t row_count, float* out, cudaStream_t stream);
+
+// argmax over an fp32 vector already in device memory (first index on ties).
+cudaError_t launch_argmax(const float* v, uint64_t n, ArgmaxScratch* scratch, int num_sms, cudaStream_t stream);
+
+uint64_t row_bytes_of(uint32_t type, uint64_t cols);
+
+}  // namespace nedo_gpu

@@ -1,0 +1,417 @@
+// nedo_gpu.cu -- the C ABI declared in include/nedo_gpu.h.
+//
+// Host-side responsibilities: argument checks with the reference's error
+// semantics (src/kernels.cpp:162-176, src/gguf.cpp:106-114), per-device state
+// (SM count, status word, argmax scratch, pinned staging), the weight
+// residency cache for the host-pointer entry points, and the choice between
+// the streaming kernel, the batched tensor-core kernel and the generic kernel.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/nedo_gpu.h"
+#include "common.cuh"
+#include "launch.h"
+
+using namespace nedo_gpu;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+    return fail(e == cudaErrorMemoryAllocation ? NEDO_GPU_ERR_NOMEM : NEDO_GPU_ERR_CUDA, m);
+}
+
+#define NEDO_CUDA_TRY(call)                                  \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+    } while (0)
+
+struct Resident {
+    void* dev = nullptr;
+    uint64_t bytes = 0;
+};
+
+struct DeviceState {
+    int device = -1;
+    int num_sms = 0;
+    int max_smem = 0;
+    DeviceStatus* status = nullptr;  // device memory
+    ArgmaxScratch scratch{};
+    cudaStream_t stream = nullptr;   // for the host-pointer entry points
+    float* x_dev = nullptr;
+    float* y_dev = nullptr;
+    uint64_t x_cap = 0, y_cap = 0;
+    float* x_pin = nullptr;
+    float* y_pin = nullptr;
+    uint64_t xp_cap = 0, yp_cap = 0;
+    DeviceStatus* status_pin = nullptr;
+    std::unordered_map<const void*, Resident> cache;
+    std::mutex mu;
+};
+
+std::mutex g_states_mu;
+std::vector<DeviceState*> g_states;
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    return 0;
+}
+
+int get_state(DeviceState** out) {
+    int dev = 0;
+    if (int rc = current_device(&dev)) return rc;
+    std::lock_guard<std::mutex> lk(g_states_mu);
+    if (static_cast<int>(g_states.size()) <= dev) g_states.resize(dev + 1, nullptr);
+    if (g_states[dev] != nullptr) {
+        *out = g_states[dev];
+        return 0;
+    }
+    auto* s = new DeviceState();
+    s->device = dev;
+    NEDO_CUDA_TRY(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, dev));
+    NEDO_CUDA_TRY(cudaDeviceGetAttribute(&s->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    NEDO_CUDA_TRY(cudaMalloc(&s->status, sizeof(DeviceStatus)));
+    NEDO_CUDA_TRY(cudaMemset(s->status, 0, sizeof(DeviceStatus)));
+    const size_t n = static_cast<size_t>(s->num_sms) + 1;
+    NEDO_CUDA_TRY(cudaMalloc(&s->scratch.cand_val, n * sizeof(float)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->scratch.cand_idx, n * sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->scratch.counter, sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaMemset(s->scratch.counter, 0, sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    NEDO_CUDA_TRY(cudaHostAlloc(&s->status_pin, sizeof(DeviceStatus), cudaHostAllocDefault));
+    g_states[dev] = s;
+    *out = s;
+    return 0;
+}
+
+bool is_matvec_type(uint32_t t) { return t == kF16 || t == kQ4_0 || t == kQ8_0; }
+
+// tensor_nbytes semantics (src/gguf.cpp:106-114) for the types it knows.
+int tensor_row_bytes(uint32_t type, uint64_t cols, uint64_t* rb) {
+    switch (type) {
+        case 0: *rb = cols * 4; return 0;                      // F32
+        case 1: *rb = cols * 2; return 0;                      // F16
+        case 30: *rb = cols * 2; return 0;                     // BF16
+        case 2:
+            if (cols % 32) return fail(NEDO_GPU_ERR_ALIGN, "Q4_0 elements not block aligned");
+            *rb = cols / 32 * 18;
+            return 0;
+        case 8:
+            if (cols % 32) return fail(NEDO_GPU_ERR_ALIGN, "Q8_0 elements not block aligned");
+            *rb = cols / 32 * 34;
+            return 0;
+        case 24: *rb = cols; return 0;      // I8
+        case 25: *rb = cols * 2; return 0;  // I16
+        case 26: *rb = cols * 4; return 0;  // I32
+        case 27: *rb = cols * 8; return 0;  // I64
+        default: return fail(NEDO_GPU_ERR_TYPE, "tensor type not implemented: " + std::to_string(type));
+    }
+}
+
+int check_matvec_args(uint32_t type, uint64_t rows, uint64_t cols, uint64_t* rb) {
+    if (int rc = tensor_row_bytes(type, cols, rb)) return rc;
+    if (rows > 0 && !is_matvec_type(type)) return fail(NEDO_GPU_ERR_TYPE, "matvec tensor type not supported");
+    if (rows > 0xFFFFFFFFull) return fail(NEDO_GPU_ERR_ARG, "matvec: more than 2^32-1 rows");
+    return 0;
+}
+
+template <typename T>
+int ensure_dev(T** p, uint64_t* cap, uint64_t need) {
+    if (*cap >= need) return 0;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), need * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    *cap = need;
+    return 0;
+}
+
+template <typename T>
+int ensure_pin(T** p, uint64_t* cap, uint64_t need) {
+    if (*cap >= need) return 0;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(p), need * sizeof(T), cudaHostAllocDefault);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(staging)");
+    *cap = need;
+    return 0;
+}
+
+int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const void** w_dev) {
+    auto it = s->cache.find(w_host);
+    if (it != s->cache.end() && it->second.bytes == w_bytes) {
+        *w_dev = it->second.dev;
+        return 0;
+    }
+    if (it != s->cache.end()) {
+        cudaFree(it->second.dev);
+        s->cache.erase(it);
+    }
+    void* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, w_bytes ? w_bytes : 16);
+    if (e == cudaErrorMemoryAllocation) {
+        // Out of room: drop every other resident weight and retry once.
+        cudaGetLastError();
+        for (auto& kv : s->cache) cudaFree(kv.second.dev);
+        s->cache.clear();
+        e = cudaMalloc(&d, w_bytes ? w_bytes : 16);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight)");
+    if (w_bytes) {
+        e = cudaMemcpy(d, w_host, w_bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(d);
+            return cuda_fail(e, "cudaMemcpy(weight upload)");
+        }
+    }
+    s->cache[w_host] = Resident{d, w_bytes};
+    *w_dev = d;
+    return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The one dispatch point for every matvec launch.
+int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
+                    float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream) {
+    if (rows == 0 || batch == 0) return 0;
+    if (batch == 1 && aligned16(w) && aligned16(x)) {
+        StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
+        if (plan.ok) {
+            cudaError_t e = launch_stream(type, plan, w, x, y, rows, cols, s->status, amax, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
+            return 0;
+        }
+    }
+    if (batch > 1 && aligned16(w) && aligned16(x) && (cols * sizeof(float)) % 16 == 0) {
+        StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
+        if (plan.ok) {
+            for (uint32_t b = 0; b < batch; ++b) {
+                cudaError_t e = launch_stream(type, plan, w, x + static_cast<uint64_t>(b) * cols,
+                                              y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, nullptr,
+                                              stream);
+                if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
+            }
+            return 0;
+        }
+    }
+    cudaError_t e = launch_generic(type, w, x, y, rows, cols, batch, cols, rows, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_generic launch");
+    if (amax) {
+        e = launch_argmax(y, rows, const_cast<ArgmaxScratch*>(amax), s->num_sms, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+    }
+    return 0;
+}
+
+int read_status(DeviceState* s, cudaStream_t stream) {
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->status_pin, s->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, stream));
+    NEDO_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (s->status_pin->flags != 0) {
+        const DeviceStatus st = *s->status_pin;
+        cudaMemsetAsync(s->status, 0, sizeof(DeviceStatus), stream);
+        cudaStreamSynchronize(stream);
+        char buf[160];
+        std::snprintf(buf, sizeof(buf), "device kernel gave up on a bounded wait (flags=0x%x, site=%u)", st.flags,
+                      st.where);
+        return fail(NEDO_GPU_ERR_DEVICE, buf);
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nedo_gpu_version(void) { return 100; }
+
+const char* nedo_gpu_last_error(void) { return g_last_error.c_str(); }
+
+int nedo_gpu_matvec(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                    const float* x_host, float* y_host) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0) return 0;
+    if (!w_host || !x_host || !y_host) return fail(NEDO_GPU_ERR_ARG, "matvec: null pointer");
+    if (w_bytes < rows * rb) return fail(NEDO_GPU_ERR_ARG, "matvec: weight span shorter than rows * row_bytes");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    const void* w_dev = nullptr;
+    if (int rc = resident_weight(s, w_host, w_bytes, &w_dev)) return rc;
+    if (int rc = ensure_dev(&s->x_dev, &s->x_cap, cols)) return rc;
+    if (int rc = ensure_dev(&s->y_dev, &s->y_cap, rows)) return rc;
+    if (int rc = ensure_pin(&s->x_pin, &s->xp_cap, cols)) return rc;
+    if (int rc = ensure_pin(&s->y_pin, &s->yp_cap, rows)) return rc;
+    std::memcpy(s->x_pin, x_host, cols * sizeof(float));
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->x_dev, s->x_pin, cols * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, 1, nullptr, s->stream)) return rc;
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->y_pin, s->y_dev, rows * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (int rc = read_status(s, s->stream)) return rc;
+    std::memcpy(y_host, s->y_pin, rows * sizeof(float));
+    return 0;
+}
+
+int nedo_gpu_embedding_row(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                           uint32_t row, float* out_host) {
+    if (row >= rows) return fail(NEDO_GPU_ERR_ROW, "bad embedding row");
+    uint64_t rb = 0;
+    if (int rc = tensor_row_bytes(type, cols, &rb)) return rc;
+    if (!is_matvec_type(type)) return fail(NEDO_GPU_ERR_TYPE, "embedding type unsupported");
+    if (!w_host || !out_host) return fail(NEDO_GPU_ERR_ARG, "embedding_row: null pointer");
+    if (w_bytes < rows * rb) return fail(NEDO_GPU_ERR_ARG, "embedding_row: weight span shorter than rows * row_bytes");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    const void* w_dev = nullptr;
+    if (int rc = resident_weight(s, w_host, w_bytes, &w_dev)) return rc;
+    if (int rc = ensure_dev(&s->y_dev, &s->y_cap, cols)) return rc;
+    if (int rc = ensure_pin(&s->y_pin, &s->yp_cap, cols)) return rc;
+    cudaError_t e = launch_dequant_rows(type, w_dev, rows, cols, row, 1, s->y_dev, s->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->y_pin, s->y_dev, cols * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    NEDO_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    std::memcpy(out_host, s->y_pin, cols * sizeof(float));
+    return 0;
+}
+
+int nedo_gpu_weight_upload(const void* w_host, uint64_t w_bytes, const void** w_dev_out) {
+    if (!w_host || !w_dev_out) return fail(NEDO_GPU_ERR_ARG, "weight_upload: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    return resident_weight(s, w_host, w_bytes, w_dev_out);
+}
+
+int nedo_gpu_weight_evict(const void* w_host) {
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    auto it = s->cache.find(w_host);
+    if (it != s->cache.end()) {
+        cudaFree(it->second.dev);
+        s->cache.erase(it);
+    }
+    return 0;
+}
+
+int nedo_gpu_cache_clear(void) {
+    std::lock_guard<std::mutex> lk(g_states_mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (DeviceState* s : g_states) {
+        if (s == nullptr) continue;
+        std::lock_guard<std::mutex> lk2(s->mu);
+        cudaSetDevice(s->device);
+        for (auto& kv : s->cache) cudaFree(kv.second.dev);
+        s->cache.clear();
+    }
+    cudaSetDevice(prev);
+    return 0;
+}
+
+int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
+                        float* y_dev, uint32_t batch, void* stream) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0 || batch == 0) return 0;
+    if (!w_dev || !x_dev || !y_dev) return fail(NEDO_GPU_ERR_ARG, "matvec_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    return dispatch_matvec(s, type, rows, cols, w_dev, x_dev, y_dev, batch, nullptr,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int nedo_gpu_matvec_argmax_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
+                               float* y_dev, int64_t* index_dev, float* value_dev, void* stream) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0) return fail(NEDO_GPU_ERR_ARG, "argmax of an empty vector");
+    if (!w_dev || !x_dev || !y_dev || !index_dev) return fail(NEDO_GPU_ERR_ARG, "matvec_argmax_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    ArgmaxScratch a = s->scratch;
+    a.out_index = index_dev;
+    a.out_value = value_dev;
+    return dispatch_matvec(s, type, rows, cols, w_dev, x_dev, y_dev, 1, &a, static_cast<cudaStream_t>(stream));
+}
+
+int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev, void* stream) {
+    if (n == 0) return fail(NEDO_GPU_ERR_ARG, "argmax of an empty vector");
+    if (n > 0xFFFFFFFFull) return fail(NEDO_GPU_ERR_ARG, "argmax: more than 2^32-1 elements");
+    if (!v_dev || !index_dev) return fail(NEDO_GPU_ERR_ARG, "argmax_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    ArgmaxScratch a = s->scratch;
+    a.out_index = index_dev;
+    a.out_value = value_dev;
+    cudaError_t e = launch_argmax(v_dev, n, &a, s->num_sms, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+    return 0;
+}
+
+int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, uint64_t row_begin,
+                              uint64_t row_count, float* out_dev, void* stream) {
+    if (row_begin >= rows || row_count > rows - row_begin) return fail(NEDO_GPU_ERR_ROW, "bad embedding row");
+    uint64_t rb = 0;
+    if (int rc = tensor_row_bytes(type, cols, &rb)) return rc;
+    if (!is_matvec_type(type)) return fail(NEDO_GPU_ERR_TYPE, "embedding type unsupported");
+    if (!w_dev || !out_dev) return fail(NEDO_GPU_ERR_ARG, "dequant_rows_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    cudaError_t e = launch_dequant_rows(type, w_dev, rows, cols, row_begin, row_count, out_dev,
+                                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+    return 0;
+}
+
+int nedo_gpu_status(void* stream) {
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    return read_status(s, static_cast<cudaStream_t>(stream));
+}
+
+int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n) {
+    if (!out || n < 8) return fail(NEDO_GPU_ERR_ARG, "plan_info: need 8 output slots");
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
+    if (batch <= 1) {
+        StreamPlan p = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
+        if (p.ok) {
+            out[0] = 1;
+            out[1] = p.grid;
+            out[2] = p.threads;
+            out[3] = p.smem_bytes;
+            out[4] = p.rows_per_tile;
+            out[5] = p.stages;
+            out[6] = p.chunks;
+            out[7] = p.groups;
+            return 0;
+        }
+    }
+    out[0] = 2;
+    return 0;
+}
+
+}  // extern "C"

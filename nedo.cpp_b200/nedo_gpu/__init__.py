@@ -1,0 +1,166 @@
+"""Python host binding of libnedo_gpu.so (the C ABI in include/nedo_gpu.h).
+
+The reference exposes this path as C++ (``nedo::kernels::matvec`` /
+``embedding_row``, include/nedo/kernels.hpp:20-21); the functions here mirror
+those two calls -- same argument meaning (GGUF type code, ``cols`` = shape[0]
+contiguous, ``rows`` = shape[1]) and the same error messages -- for tests,
+benchmarks and Python callers.  There is no CPU fallback: importing this module
+without the built library raises.
+
+Host-pointer calls (``matvec``, ``embedding_row``) take numpy arrays and are
+synchronous.  Device calls (``matvec_dev`` ...) take raw device addresses (for
+example ``torch.Tensor.data_ptr()``) and a CUDA stream handle, and are
+asynchronous on that stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import blocks
+from .blocks import F16, Q4_0, Q8_0, row_bytes
+
+__all__ = ["F16", "Q4_0", "Q8_0", "row_bytes", "blocks", "Library", "load", "NedoGpuError", "LIB_PATH"]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_DIR = os.path.join(os.path.dirname(HERE), "lib")
+LIB_PATH = os.path.join(LIB_DIR, "libnedo_gpu.so")
+
+OK, ERR_TYPE, ERR_ALIGN, ERR_ROW, ERR_ARG, ERR_CUDA, ERR_DEVICE, ERR_NOMEM = range(8)
+
+# Every symbol include/nedo_gpu.h declares (checked by the CPU test suite).
+EXPORTS = (
+    "nedo_gpu_version",
+    "nedo_gpu_last_error",
+    "nedo_gpu_matvec",
+    "nedo_gpu_embedding_row",
+    "nedo_gpu_weight_upload",
+    "nedo_gpu_weight_evict",
+    "nedo_gpu_cache_clear",
+    "nedo_gpu_matvec_dev",
+    "nedo_gpu_matvec_argmax_dev",
+    "nedo_gpu_argmax_dev",
+    "nedo_gpu_dequant_rows_dev",
+    "nedo_gpu_status",
+    "nedo_gpu_plan_info",
+)
+
+
+class NedoGpuError(RuntimeError):
+    """A non-zero status from the C ABI; ``code`` is the NEDO_GPU_ERR_* value."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+_u32, _u64, _i32, _vp = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+_SIGNATURES = {
+    "nedo_gpu_version": ([], _i32),
+    "nedo_gpu_last_error": ([], ctypes.c_char_p),
+    "nedo_gpu_matvec": ([_u32, _u64, _u64, _vp, _u64, _vp, _vp], _i32),
+    "nedo_gpu_embedding_row": ([_u32, _u64, _u64, _vp, _u64, _u32, _vp], _i32),
+    "nedo_gpu_weight_upload": ([_vp, _u64, ctypes.POINTER(_vp)], _i32),
+    "nedo_gpu_weight_evict": ([_vp], _i32),
+    "nedo_gpu_cache_clear": ([], _i32),
+    "nedo_gpu_matvec_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _u32, _vp], _i32),
+    "nedo_gpu_matvec_argmax_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
+    "nedo_gpu_argmax_dev": ([_vp, _u64, _vp, _vp, _vp], _i32),
+    "nedo_gpu_dequant_rows_dev": ([_u32, _u64, _u64, _vp, _u64, _u64, _vp, _vp], _i32),
+    "nedo_gpu_status": ([_vp], _i32),
+    "nedo_gpu_plan_info": ([_u32, _u64, _u64, _u32, ctypes.POINTER(_u32), _i32], _i32),
+}
+
+
+class Library:
+    """ctypes view of libnedo_gpu.so with checked calls."""
+
+    def __init__(self, path: str = LIB_PATH):
+        if not os.path.exists(path):
+            raise FileNotFoundError(
+                f"{path} is missing: build it with `make -C nedo.cpp_b200` (there is no CPU fallback)")
+        self.path = path
+        self.lib = ctypes.CDLL(path)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(self.lib, name)
+            fn.argtypes = args
+            fn.restype = res
+
+    # ------------------------------------------------------------------ utils
+    def version(self) -> int:
+        return self.lib.nedo_gpu_version()
+
+    def last_error(self) -> str:
+        return self.lib.nedo_gpu_last_error().decode()
+
+    def _check(self, rc: int) -> None:
+        if rc != OK:
+            raise NedoGpuError(rc, self.last_error())
+
+    # ------------------------------------------------------- host entry points
+    def matvec(self, type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+        """nedo::kernels::matvec: y[r] = dot(row r, x).  w holds the GGUF bytes."""
+        w = np.ascontiguousarray(w)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty(rows, dtype=np.float32)
+        self._check(self.lib.nedo_gpu_matvec(type_, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data,
+                                             y.ctypes.data))
+        return y
+
+    def embedding_row(self, type_: int, rows: int, cols: int, w: np.ndarray, row: int) -> np.ndarray:
+        """nedo::kernels::embedding_row: the dequantised row (bit-exact)."""
+        w = np.ascontiguousarray(w)
+        out = np.empty(cols, dtype=np.float32)
+        self._check(self.lib.nedo_gpu_embedding_row(type_, rows, cols, w.ctypes.data, w.nbytes, row,
+                                                    out.ctypes.data))
+        return out
+
+    def weight_upload(self, w: np.ndarray) -> int:
+        ptr = _vp()
+        self._check(self.lib.nedo_gpu_weight_upload(w.ctypes.data, w.nbytes, ctypes.byref(ptr)))
+        return ptr.value
+
+    def weight_evict(self, w: np.ndarray) -> None:
+        self._check(self.lib.nedo_gpu_weight_evict(w.ctypes.data))
+
+    def cache_clear(self) -> None:
+        self._check(self.lib.nedo_gpu_cache_clear())
+
+    # ----------------------------------------------------- device entry points
+    def matvec_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, batch=1, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_matvec_dev(type_, rows, cols, w_ptr, x_ptr, y_ptr, batch, stream))
+
+    def matvec_argmax_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, index_ptr, value_ptr=None, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_matvec_argmax_dev(type_, rows, cols, w_ptr, x_ptr, y_ptr, index_ptr,
+                                                        value_ptr, stream))
+
+    def argmax_dev(self, v_ptr, n, index_ptr, value_ptr=None, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_argmax_dev(v_ptr, n, index_ptr, value_ptr, stream))
+
+    def dequant_rows_dev(self, type_, rows, cols, w_ptr, row_begin, row_count, out_ptr, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_dequant_rows_dev(type_, rows, cols, w_ptr, row_begin, row_count, out_ptr,
+                                                       stream))
+
+    def status(self, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_status(stream))
+
+    def plan_info(self, type_, rows, cols, batch=1) -> dict:
+        out = (_u32 * 8)()
+        self._check(self.lib.nedo_gpu_plan_info(type_, rows, cols, batch, out, 8))
+        keys = ("path", "grid", "threads", "smem_bytes", "rows_per_tile", "stages", "chunks", "groups")
+        return dict(zip(keys, list(out)))
+
+
+_LIB: Library | None = None
+
+
+def load(path: str = LIB_PATH) -> Library:
+    """The process-wide Library (loaded once)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = Library(path)
+    return _LIB
