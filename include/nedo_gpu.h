@@ -64,6 +64,14 @@ enum {
 /* Library version: major*10000 + minor*100 + patch. */
 NEDO_GPU_API int nedo_gpu_version(void);
 
+/* Programmatic dependent launch for the device entry points (process-wide,
+ * off by default).  When on, a matvec kernel starts streaming its weight
+ * while the previous kernel on the same stream is still running and reads x
+ * only once that kernel has completed.  Contract: the weight must not be
+ * written by the kernel launched immediately before on that stream (GGUF
+ * weights are immutable).  Returns the previous setting. */
+NEDO_GPU_API int nedo_gpu_set_pdl(int enable);
+
 /* Message of the last failing call on this thread ("" if none). */
 NEDO_GPU_API const char* nedo_gpu_last_error(void);
 
@@ -136,8 +144,8 @@ NEDO_GPU_API int nedo_gpu_status(void* stream);
 
 /* Describe the kernel choice for a shape: out[0] = path (1 streaming,
  * 2 generic, 3 batched tensor-core), out[1] grid, out[2] threads,
- * out[3] dynamic shared bytes, out[4] rows per tile, out[5] stages,
- * out[6] chunks, out[7] groups.  n = capacity of out (>= 8). */
+ * out[3] dynamic shared bytes, out[4] rows per tile, out[5] ring slots per
+ * warp, out[6] slot bytes, out[7] warps per CTA.  n = capacity of out (>= 8). */
 NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
 
 #ifdef __cplusplus

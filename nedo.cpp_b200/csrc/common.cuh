@@ -57,14 +57,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps (up to ~0.5 us)
+// instead of spinning on issue slots the computing warps need.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(500u)
         : "memory");
     return ok != 0;
 }
@@ -98,6 +100,13 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         : "memory");
 }
 
+// L2 policy for data many CTAs read (the activation vector).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // L2 policy for data read exactly once (the weight stream).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
@@ -128,8 +137,12 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return d;
 }
 
+// (a & mask) | bits as a single LOP3 with all three operands in registers
+// (two 32-bit immediates do not fit one instruction).
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t bits) {
-    return (a & mask) | bits;  // one LOP3
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(bits));
+    return d;
 }
 
 }  // namespace nedo_gpu

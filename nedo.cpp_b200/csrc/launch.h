@@ -21,25 +21,37 @@ struct ArgmaxScratch {
 
 struct StreamPlan {
     bool ok = false;
-    uint32_t chunks = 0;         // warps that split one row's columns
-    uint32_t groups = 0;         // independent row groups per CTA
-    uint32_t rows_per_tile = 0;  // rows moved by one bulk copy
-    uint32_t stages = 0;         // ring depth
-    uint32_t stage_bytes = 0;
+    uint32_t warps = 0;          // per CTA; every warp streams its own row range
+    uint32_t rows_per_tile = 0;  // rows moved per tile (one contiguous byte range)
+    uint32_t slots = 0;          // ring slots per warp
+    uint32_t slot_bytes = 0;
+    uint32_t x_bytes = 0;        // shared memory for the staged activations
+    uint32_t piece_bytes = 0;    // bytes per bulk copy
     uint32_t threads = 0;
     uint32_t smem_bytes = 0;
     uint32_t grid = 0;
-    uint64_t tiles = 0;
 };
 
-StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin);
+// Optional overrides of the planner's choices (0 = planner default).
+struct StreamTuning {
+    uint32_t warps = 0;
+    uint32_t slots = 0;
+    uint32_t tile_bytes = 0;
+    uint32_t piece_bytes = 0;
+    uint32_t smem_budget = 0;
+};
+
+StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
+                       const StreamTuning* tune = nullptr);
 
 // Batch-1 streaming GEMV over GGUF bytes.  w/x/y are device pointers on the
-// current device.  When `amax` is non-null (F16 only) the argmax of y is also
-// produced, first index on ties.
+// current device.  When `amax` is non-null the argmax of y is also produced
+// (first index on ties).  `pdl` launches with programmatic stream
+// serialisation: the kernel starts streaming its weight while the previous
+// kernel on the stream finishes, and reads x only after that kernel completed.
 cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, const float* x, float* y,
                           uint64_t rows, uint64_t cols, DeviceStatus* status, const ArgmaxScratch* amax,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool pdl);
 
 // Any shape the streaming kernel does not take (odd row sizes, unaligned
 // pointers): one warp per row, byte-granular loads.  x is [batch][ldx], y [batch][ldy].

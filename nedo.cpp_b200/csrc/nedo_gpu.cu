@@ -9,6 +9,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -66,6 +67,7 @@ struct DeviceState {
 
 std::mutex g_states_mu;
 std::vector<DeviceState*> g_states;
+std::atomic<int> g_pdl{0};
 
 int current_device(int* dev) {
     cudaError_t e = cudaGetDevice(dev);
@@ -196,7 +198,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
     if (batch == 1 && aligned16(w) && aligned16(x)) {
         StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
         if (plan.ok) {
-            cudaError_t e = launch_stream(type, plan, w, x, y, rows, cols, s->status, amax, stream);
+            cudaError_t e = launch_stream(type, plan, w, x, y, rows, cols, s->status, amax, stream, g_pdl.load() != 0);
             if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
             return 0;
         }
@@ -207,7 +209,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             for (uint32_t b = 0; b < batch; ++b) {
                 cudaError_t e = launch_stream(type, plan, w, x + static_cast<uint64_t>(b) * cols,
                                               y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, nullptr,
-                                              stream);
+                                              stream, g_pdl.load() != 0);
                 if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
             }
             return 0;
@@ -242,6 +244,11 @@ int read_status(DeviceState* s, cudaStream_t stream) {
 extern "C" {
 
 int nedo_gpu_version(void) { return 100; }
+
+int nedo_gpu_set_pdl(int enable) {
+    const int prev = g_pdl.exchange(enable != 0 ? 1 : 0);
+    return prev;
+}
 
 const char* nedo_gpu_last_error(void) { return g_last_error.c_str(); }
 
@@ -404,9 +411,9 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             out[2] = p.threads;
             out[3] = p.smem_bytes;
             out[4] = p.rows_per_tile;
-            out[5] = p.stages;
-            out[6] = p.chunks;
-            out[7] = p.groups;
+            out[5] = p.slots;
+            out[6] = p.slot_bytes;
+            out[7] = p.warps;
             return 0;
         }
     }

@@ -33,6 +33,7 @@ OK, ERR_TYPE, ERR_ALIGN, ERR_ROW, ERR_ARG, ERR_CUDA, ERR_DEVICE, ERR_NOMEM = ran
 # Every symbol include/nedo_gpu.h declares (checked by the CPU test suite).
 EXPORTS = (
     "nedo_gpu_version",
+    "nedo_gpu_set_pdl",
     "nedo_gpu_last_error",
     "nedo_gpu_matvec",
     "nedo_gpu_embedding_row",
@@ -61,6 +62,7 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 
 _SIGNATURES = {
     "nedo_gpu_version": ([], _i32),
+    "nedo_gpu_set_pdl": ([_i32], _i32),
     "nedo_gpu_last_error": ([], ctypes.c_char_p),
     "nedo_gpu_matvec": ([_u32, _u64, _u64, _vp, _u64, _vp, _vp], _i32),
     "nedo_gpu_embedding_row": ([_u32, _u64, _u64, _vp, _u64, _u32, _vp], _i32),
@@ -93,6 +95,10 @@ class Library:
     # ------------------------------------------------------------------ utils
     def version(self) -> int:
         return self.lib.nedo_gpu_version()
+
+    def set_pdl(self, enable: bool) -> bool:
+        """Programmatic dependent launch for the device entry points; returns the old setting."""
+        return bool(self.lib.nedo_gpu_set_pdl(1 if enable else 0))
 
     def last_error(self) -> str:
         return self.lib.nedo_gpu_last_error().decode()
@@ -151,7 +157,7 @@ class Library:
     def plan_info(self, type_, rows, cols, batch=1) -> dict:
         out = (_u32 * 8)()
         self._check(self.lib.nedo_gpu_plan_info(type_, rows, cols, batch, out, 8))
-        keys = ("path", "grid", "threads", "smem_bytes", "rows_per_tile", "stages", "chunks", "groups")
+        keys = ("path", "grid", "threads", "smem_bytes", "rows_per_tile", "slots", "slot_bytes", "warps")
         return dict(zip(keys, list(out)))
 
 
