@@ -249,6 +249,9 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     lib = nedo_gpu.load()
+    # Programmatic dependent launch: each matvec starts streaming its weight
+    # while the previous launch drains (x is read only after it completed).
+    lib.set_pdl(True)
     t, cols = wl["type"], wl["cols"]
     rows, rows_total = shard_rows(wl, world)
     rb = B.row_bytes(t, cols)
@@ -357,7 +360,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         "config": dict(workload_config(args.workload, wl, world),
                        l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
                           f"> 4x L2)", graph="K steps captured as one CUDA graph" if world == 1 else "eager",
-                       plan=plan),
+                       pdl=True, plan=plan),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"

@@ -142,10 +142,11 @@ NEDO_GPU_API int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_
  * by kernels on the current device since the last check. */
 NEDO_GPU_API int nedo_gpu_status(void* stream);
 
-/* Describe the kernel choice for a shape: out[0] = path (1 streaming,
- * 2 generic, 3 batched tensor-core), out[1] grid, out[2] threads,
- * out[3] dynamic shared bytes, out[4] rows per tile, out[5] ring slots per
- * warp, out[6] slot bytes, out[7] warps per CTA.  n = capacity of out (>= 8). */
+/* Describe the kernel choice for a shape: out[0] = path (1 streaming CUDA-core,
+ * 2 generic, 3 batched tensor-core, 4 int8 tensor-pipe matvec), out[1] grid,
+ * out[2] threads, out[3] dynamic shared bytes, out[4] rows per tile,
+ * out[5] ring slots, out[6] slot bytes, out[7] warps per CTA (compute warps for
+ * path 4).  n = capacity of out (>= 8). */
 NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
 
 #ifdef __cplusplus

@@ -53,6 +53,35 @@ cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, 
                           uint64_t rows, uint64_t cols, DeviceStatus* status, const ArgmaxScratch* amax,
                           cudaStream_t stream, bool pdl);
 
+// Batch-1 Q8_0 / Q4_0 on the int8 tensor pipe (mma.sync m16n8k32, x as exact
+// int8 limbs).  Row tiles of 8 or 16 rows, each warp a fixed column slice.
+struct ImmaPlan {
+    bool ok = false;
+    uint32_t type = 0;
+    uint32_t warps = 0;       // consumer warps (column slices); one more warp streams tiles
+    uint32_t pairs = 0;       // block pairs per warp
+    uint32_t tile_rows = 0;
+    uint32_t row_stride = 0;  // padded shared-memory row pitch
+    uint32_t tiles = 0;
+    uint32_t slots = 0;
+    uint32_t slot_bytes = 0;
+    uint32_t smem_bytes = 0;
+    uint32_t grid = 0;
+};
+
+struct ImmaTuning {
+    uint32_t warps = 0;
+    uint32_t tile_rows = 0;
+    uint32_t slots = 0;
+    uint32_t piece_bytes = 0;
+    uint32_t smem_budget = 0;
+};
+
+ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
+                   const ImmaTuning* tune = nullptr);
+cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
+                        DeviceStatus* status, cudaStream_t stream, bool pdl);
+
 // Any shape the streaming kernel does not take (odd row sizes, unaligned
 // pointers): one warp per row, byte-granular loads.  x is [batch][ldx], y [batch][ldy].
 cudaError_t launch_generic(uint32_t type, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,

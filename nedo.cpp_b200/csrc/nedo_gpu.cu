@@ -195,6 +195,14 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
                     float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream) {
     if (rows == 0 || batch == 0) return 0;
+    if (batch == 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
+        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+        if (ip.ok) {
+            cudaError_t e = launch_imma(ip, w, x, y, rows, cols, s->status, stream, g_pdl.load() != 0);
+            if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch");
+            return 0;
+        }
+    }
     if (batch == 1 && aligned16(w) && aligned16(x)) {
         StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
         if (plan.ok) {
@@ -403,6 +411,20 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
+    if (batch <= 1 && (type == kQ8_0 || type == kQ4_0)) {
+        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+        if (ip.ok) {
+            out[0] = 4;
+            out[1] = ip.grid;
+            out[2] = (ip.warps + 1) * 32;
+            out[3] = ip.smem_bytes;
+            out[4] = ip.tile_rows;
+            out[5] = ip.slots;
+            out[6] = ip.slot_bytes;
+            out[7] = ip.warps;
+            return 0;
+        }
+    }
     if (batch <= 1) {
         StreamPlan p = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
         if (p.ok) {
