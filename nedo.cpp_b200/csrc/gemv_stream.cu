@@ -320,6 +320,7 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(const StreamArgs a)
     uint64_t* xbar = all_bars + a.warps * kMaxSlots;
     float* am_val = reinterpret_cast<float*>(xbar + 1);
     uint32_t* am_idx = reinterpret_cast<uint32_t*>(am_val + 32);
+    uint32_t* am_last = am_idx + 32;  // set by thread 0: this CTA finished last
 
     // this warp's rows: an even split over all warps of the grid
     const uint64_t gw = static_cast<uint64_t>(blockIdx.x) * a.warps + warp;
@@ -434,21 +435,28 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(const StreamArgs a)
         a.amax.cand_idx[blockIdx.x] = i;
         __threadfence();
         const uint32_t done = atomicAdd(a.amax.counter, 1u);
-        if (done == gridDim.x - 1u) {
-            __threadfence();
-            const volatile float* cv = a.amax.cand_val;
-            const volatile uint32_t* ci = a.amax.cand_idx;
-            float bv = cv[0];
-            uint32_t bi = ci[0];
-            for (uint32_t k = 1; k < gridDim.x; ++k)
-                if (amax_better(cv[k], ci[k], bv, bi)) {
-                    bv = cv[k];
-                    bi = ci[k];
-                }
-            *a.amax.out_index = static_cast<int64_t>(bi);
-            if (a.amax.out_value != nullptr) *a.amax.out_value = bv;
-            *a.amax.counter = 0u;  // ready for the next launch
+        *am_last = done == gridDim.x - 1u ? 1u : 0u;
+    }
+    __syncthreads();
+    if (*am_last == 0u || warp != 0) return;
+    // The last CTA to finish: warp 0 folds the per-CTA candidates, each lane a
+    // strided subset (L2 loads, independent), then across the warp.
+    __threadfence();
+    float bv = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (uint32_t k = lane; k < gridDim.x; k += 32u) {
+        const float v = __ldcg(a.amax.cand_val + k);
+        const uint32_t i = __ldcg(a.amax.cand_idx + k);
+        if (amax_better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
         }
+    }
+    warp_argmax(bv, bi);
+    if (lane == 0) {
+        *a.amax.out_index = static_cast<int64_t>(bi);
+        if (a.amax.out_value != nullptr) *a.amax.out_value = bv;
+        *a.amax.counter = 0u;  // ready for the next launch
     }
 }
 
@@ -504,6 +512,9 @@ uint64_t row_bytes_of(uint32_t type, uint64_t cols) {
     }
 }
 
+// Shared memory of the fused argmax: am_val[32], am_idx[32], am_last, padding.
+constexpr uint64_t kArgmaxSmemBytes = 272;
+
 StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
                        const StreamTuning* tune) {
     StreamPlan best;
@@ -521,7 +532,7 @@ StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms,
     const StreamTuning t = tune ? *tune : StreamTuning{};
     uint64_t budget = t.smem_budget ? t.smem_budget : static_cast<uint64_t>(max_smem_optin);
     if (budget > static_cast<uint64_t>(max_smem_optin)) budget = max_smem_optin;
-    const uint64_t misc = align_up(cols * 4u, 128) + 8u * kMaxSlots * 16u + 8u + 256u;
+    const uint64_t misc = align_up(cols * 4u, 128) + 8u * kMaxSlots * 16u + 8u + kArgmaxSmemBytes;
     if (x_bytes + misc >= budget) return best;
 
     auto make = [&](uint32_t warps, uint32_t r, uint32_t slots, uint32_t grid) {
@@ -535,11 +546,24 @@ StreamPlan plan_stream(uint32_t type, uint64_t rows, uint64_t cols, int num_sms,
         p.threads = warps * 32u;
         p.grid = grid;
         const uint64_t smem = x_bytes + align_up(cols * 4u, 128) + static_cast<uint64_t>(warps) * slots * p.slot_bytes +
-                              8u * kMaxSlots * warps + 8u + 256u;
+                              8u * kMaxSlots * warps + 8u + kArgmaxSmemBytes;
         p.smem_bytes = static_cast<uint32_t>(smem);
         p.ok = smem <= budget;
         return p;
     };
+    // F16 is HBM bound: what matters is the size of each bulk copy (>= 8 KB) and
+    // enough of them in flight; 8 warps with 2 slots each measured best on
+    // 128000x2048 and 32000x4096 heads.
+    if (type == kF16 && !tune) {
+        uint32_t grid = static_cast<uint32_t>(num_sms);
+        if (static_cast<uint64_t>(grid) * 8u > rows) grid = static_cast<uint32_t>((rows + 7u) / 8u);
+        const uint64_t rpw = (rows + static_cast<uint64_t>(grid) * 8u - 1) / (static_cast<uint64_t>(grid) * 8u);
+        uint64_t r = (8192u + rb - 1) / rb;
+        if (r > kMaxRowsPerTile) r = kMaxRowsPerTile;
+        if (r > rpw) r = rpw;
+        const StreamPlan p = make(8u, static_cast<uint32_t>(r), r >= rpw ? 1u : 2u, grid);
+        if (p.ok) return p;
+    }
     // Score: expected time ~ (rows actually computed per warp) with a penalty
     // for streaming tiles (x re-read per tile).  Lower is better.
     double best_score = 1e300;
