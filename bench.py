@@ -57,7 +57,10 @@ WORKLOADS = {
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures
 # summarised under profiles/ (None where no capture exists for the workload).
-NCU_TRAFFIC_BYTES = {}
+NCU_TRAFFIC_BYTES = {
+    "q4_0_11008x4096": 25_426_432,  # profiles/gemv_imma_q4_0_11008x4096.md
+    "q8_0_4096x4096": 17_874_688,   # profiles/gemv_imma_q8_0_4096x4096.md
+}
 
 
 def env_int(name, default):
@@ -355,7 +358,9 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-        "scaling": "weak" if wl["shard"] == "weak" else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if wl["shard"] == "weak" else "strong", "vs_baseline": None,
+        # block dots on the int8 tensor pipe (exact int32) for the IMMA plan, fp32 FMA otherwise
+        "dtype": "int8" if plan.get("path") == 4 else "f32",
         "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
         "config": dict(workload_config(args.workload, wl, world),
                        l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
