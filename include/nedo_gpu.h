@@ -133,6 +133,18 @@ NEDO_GPU_API int nedo_gpu_matvec_argmax_dev(uint32_t type, uint64_t rows, uint64
 /* argmax of an fp32 vector in device memory (first index of the maximum). */
 NEDO_GPU_API int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev, void* stream);
 
+/* nedo_gpu_argmax_dev without any allocation: the same kernel and result,
+ * with its per-CTA candidates and completion counter in a fixed 8448-byte
+ * __device__ array of the library (room for 1024 CTAs; a launch needing more
+ * returns NEDO_GPU_ERR_ARG) instead of the per-device scratch that the other
+ * entry points allocate on first use.  No reference counterpart: the
+ * reference picks the token on the host (std::max_element, src/model.cpp:36).
+ * The first call on a device resolves the array's address; make it outside
+ * stream capture.  Calls that may overlap on one device (other streams, other
+ * threads) share the array and race: serialise them. */
+NEDO_GPU_API int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev,
+                                void* stream);
+
 /* embedding_row for rows [row_begin, row_begin + row_count) into
  * out_dev[row_count][cols]; bit-identical to the reference. */
 NEDO_GPU_API int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, uint64_t row_begin,

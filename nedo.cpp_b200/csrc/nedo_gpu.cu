@@ -247,6 +247,45 @@ int read_status(DeviceState* s, cudaStream_t stream) {
     return 0;
 }
 
+// ---- argmax without any allocation --------------------------------------
+// The per-CTA candidates and the completion counter of the argmax kernel live
+// in this file-scope array instead of the per-device cudaMalloc'd scratch.
+// Layout: cand_val[kNoAllocMaxCtas] (float), cand_idx[kNoAllocMaxCtas]
+// (uint32), counter (uint32, padded to 256 bytes).  Only the counter must be
+// zero before a launch: the array is zero at module load and the last CTA of
+// every launch resets the counter to zero.
+constexpr uint32_t kNoAllocMaxCtas = 1024;
+constexpr size_t kNoAllocScratchBytes = 2u * kNoAllocMaxCtas * 4u + 256u;  // 8448
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocSlot {
+    uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocSlot g_noalloc[kNoAllocMaxDevices];
+
+// Once per device: resolve the scratch address and the SM count.
+int noalloc_setup(NoAllocSlot* out) {
+    int dev = 0;
+    if (int rc = current_device(&dev)) return rc;
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(NEDO_GPU_ERR_DEVICE, "argmax_dev_noalloc: device ordinal above 63");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocSlot& s = g_noalloc[dev];
+    if (s.scratch == nullptr) {
+        int sms = 0;
+        NEDO_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        void* p = nullptr;
+        NEDO_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        s.num_sms = sms;
+        s.scratch = static_cast<uint8_t*>(p);
+    }
+    *out = s;
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -379,6 +418,31 @@ int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* index_dev, floa
     a.out_index = index_dev;
     a.out_value = value_dev;
     cudaError_t e = launch_argmax(v_dev, n, &a, s->num_sms, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+    return 0;
+}
+
+int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev,
+                                void* stream) {
+    if (n == 0) return fail(NEDO_GPU_ERR_ARG, "argmax of an empty vector");
+    if (n > 0xFFFFFFFFull) return fail(NEDO_GPU_ERR_ARG, "argmax: more than 2^32-1 elements");
+    if (!v_dev || !index_dev) return fail(NEDO_GPU_ERR_ARG, "argmax_dev_noalloc: null pointer");
+    NoAllocSlot s;
+    if (int rc = noalloc_setup(&s)) return rc;
+    // the same CTA count as launch_argmax: one candidate slot per CTA
+    uint64_t ctas = (n + 1023) / 1024;
+    if (ctas > static_cast<uint64_t>(s.num_sms)) ctas = static_cast<uint64_t>(s.num_sms);
+    if (ctas > kNoAllocMaxCtas)
+        return fail(NEDO_GPU_ERR_ARG, "argmax_dev_noalloc: needs " + std::to_string(ctas) +
+                                          " candidate slots, the static scratch holds " +
+                                          std::to_string(kNoAllocMaxCtas));
+    ArgmaxScratch a{};
+    a.cand_val = reinterpret_cast<float*>(s.scratch);
+    a.cand_idx = reinterpret_cast<uint32_t*>(s.scratch + kNoAllocMaxCtas * 4u);
+    a.counter = reinterpret_cast<uint32_t*>(s.scratch + 2u * kNoAllocMaxCtas * 4u);
+    a.out_index = index_dev;
+    a.out_value = value_dev;
+    cudaError_t e = launch_argmax(v_dev, n, &a, s.num_sms, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
     return 0;
 }

@@ -43,6 +43,7 @@ EXPORTS = (
     "nedo_gpu_matvec_dev",
     "nedo_gpu_matvec_argmax_dev",
     "nedo_gpu_argmax_dev",
+    "nedo_gpu_argmax_dev_noalloc",
     "nedo_gpu_dequant_rows_dev",
     "nedo_gpu_status",
     "nedo_gpu_plan_info",
@@ -72,6 +73,7 @@ _SIGNATURES = {
     "nedo_gpu_matvec_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _u32, _vp], _i32),
     "nedo_gpu_matvec_argmax_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev": ([_vp, _u64, _vp, _vp, _vp], _i32),
+    "nedo_gpu_argmax_dev_noalloc": ([_vp, _u64, _vp, _vp, _vp], _i32),
     "nedo_gpu_dequant_rows_dev": ([_u32, _u64, _u64, _vp, _u64, _u64, _vp, _vp], _i32),
     "nedo_gpu_status": ([_vp], _i32),
     "nedo_gpu_plan_info": ([_u32, _u64, _u64, _u32, ctypes.POINTER(_u32), _i32], _i32),
@@ -146,6 +148,11 @@ class Library:
 
     def argmax_dev(self, v_ptr, n, index_ptr, value_ptr=None, stream=0) -> None:
         self._check(self.lib.nedo_gpu_argmax_dev(v_ptr, n, index_ptr, value_ptr, stream))
+
+    def argmax_dev_noalloc(self, v_ptr, n, index_ptr, value_ptr=None, stream=0) -> None:
+        """argmax_dev with no allocation (a fixed device array of the library;
+        overlapping calls on one device race; first call outside stream capture)."""
+        self._check(self.lib.nedo_gpu_argmax_dev_noalloc(v_ptr, n, index_ptr, value_ptr, stream))
 
     def dequant_rows_dev(self, type_, rows, cols, w_ptr, row_begin, row_count, out_ptr, stream=0) -> None:
         self._check(self.lib.nedo_gpu_dequant_rows_dev(type_, rows, cols, w_ptr, row_begin, row_count, out_ptr,
