@@ -23,10 +23,14 @@
 //                             high = 16..31), one IMMA per nibble half.
 //   B (32 x 8, col-major)   = x limbs, block-diagonal: column n = 4*block + limb.
 //   D (16 x 8, s32)         = per row, per block, per limb integer dots.
-// A warp owns a fixed slice of the columns (its x limbs stay in registers for
-// the whole kernel) and all warps of a CTA share each row tile, which one
-// producer lane streams from HBM into a shared-memory ring with
-// cp.async.bulk (no multicast).  Every wait is bounded.
+// A warp owns a fixed slice of the columns (its x limbs stay in registers while
+// the CTA streams its rows) and all warps of a CTA share each 16-row tile,
+// which a producer warp streams from HBM into a shared-memory ring with
+// cp.async.bulk (one copy per row, 16 lanes issuing; no multicast).  Rows
+// longer than 15 warps x 8 pairs are cut into column chunks processed one
+// after the other (x limbs rebuilt per chunk, y accumulated in chunk order).
+// Every wait is bounded; a CTA-wide abort flag stops every warp after the
+// first timed-out wait.
 #include <math.h>
 
 #include "common.cuh"
@@ -49,15 +53,18 @@ struct ImmaArgs {
     const float* x;
     float* y;
     uint64_t rows;
-    uint32_t cols;
     uint32_t row_bytes;
-    uint32_t row_stride;  // padded row pitch in shared memory (16 mod 32 bytes: conflict free)
-    uint32_t tiles;       // ceil(rows / tile_rows)
-    uint32_t warps;       // consumer warps (column slices)
+    uint32_t pairs_total;  // cols / 64
+    uint32_t chunk_pairs;  // block pairs per column chunk (a multiple of 4 when chunks > 1)
+    uint32_t chunks;       // column chunks, streamed one after the other
+    uint32_t row_pitch;    // shared-memory bytes per tile row, 16 mod 32 (conflict free)
+    uint32_t warps;        // consumer warps (column slices)
     uint32_t slots;
     uint32_t slot_bytes;
     DeviceStatus* status;
 };
+
+constexpr uint32_t kTileRows = 16;  // rows per tile: the M of one IMMA
 
 // x limb table in shared memory: per block 144 bytes (4 limbs x 32 int8 and
 // padding that keeps the lane loads conflict free), then per block the
@@ -224,25 +231,78 @@ __device__ __forceinline__ XPair load_xpair(const uint8_t* table, const int* bin
     return xp;
 }
 
-template <uint32_t TYPE, uint32_t TILE_ROWS, uint32_t PAIRS>
+// One 16-row tile against this warp's column slice: acc0 / acc1 collect the
+// rows of fragment rows g and g+8 (this lane's D columns).  GUARD skips the
+// pairs past `valid` (the last warp of a chunk).
+template <uint32_t TYPE, uint32_t PAIRS, bool GUARD>
+__device__ __forceinline__ void tile_dot(const uint8_t* r0p, const uint8_t* r1p, const XPair (&xs)[PAIRS], uint32_t valid,
+                                         uint32_t t, uint32_t scale_blk, float& acc0, float& acc1) {
+#pragma unroll
+    for (uint32_t p = 0; p < PAIRS; ++p) {
+        if (GUARD && p >= valid) break;
+        const uint8_t* p0 = r0p + p * Pair<TYPE>::kBytes;
+        const uint8_t* p1 = r1p + p * Pair<TYPE>::kBytes;
+        int d[4];
+        if constexpr (TYPE == kQ8_0) {
+#pragma unroll
+            for (uint32_t h = 0; h < 2; ++h) {
+                // even block: quant bytes 16h+4t.. at pair offset 2+16h+4t (2 mod 4)
+                const uint32_t o = 16u * h + 4u * t;
+                const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + o);
+                const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + o);
+                const uint32_t a0 = __funnelshift_r(e0[0], e0[1], 16);
+                const uint32_t a2 = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
+                const uint32_t a1 = __funnelshift_r(e1[0], e1[1], 16);
+                const uint32_t a3 = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
+                imma(d, a0, a1, a2, a3, xs[p].b0[h], xs[p].b1[h], h == 0, false);
+            }
+        } else {
+            // even block quant bytes 4t.. at pair offset 2+4t; odd block at 20+4t
+            const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + 4u * t);
+            const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + 4u * t);
+            const uint32_t w0 = __funnelshift_r(e0[0], e0[1], 16);
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(p0 + 20u + 4u * t);
+            const uint32_t w1 = __funnelshift_r(e1[0], e1[1], 16);
+            const uint32_t w3 = *reinterpret_cast<const uint32_t*>(p1 + 20u + 4u * t);
+            const uint32_t m = 0x0F0F0F0Fu;
+            imma(d, w0 & m, w1 & m, w2 & m, w3 & m, xs[p].b0[0], xs[p].b1[0], true, true);
+            imma(d, (w0 >> 4) & m, (w1 >> 4) & m, (w2 >> 4) & m, (w3 >> 4) & m, xs[p].b0[1], xs[p].b1[1],
+                 false, true);
+        }
+        // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
+        const int v0 = d[0] * 128 + d[1] - xs[p].offset;
+        const int v1 = d[2] * 128 + d[3] - xs[p].offset;
+        const float s0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk)) * xs[p].scale;
+        const float s1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk)) * xs[p].scale;
+        acc0 = fmaf(static_cast<float>(v0), s0, acc0);
+        acc1 = fmaf(static_cast<float>(v1), s1, acc1);
+    }
+}
+
+// MULTI: the rows are cut into more than one column chunk.
+template <uint32_t TYPE, uint32_t PAIRS, bool MULTI>
 __global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gemv_imma_kernel(const ImmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t S = a.slots, W = a.warps;
-    const uint32_t nblocks = a.cols / 32u;
-    // [ring: S slots of TILE_ROWS padded rows][limb table][block info][barriers][partial sums]
+    const uint32_t table_blocks = 2u * a.chunk_pairs;  // limb table capacity (one chunk)
+    // [ring: S slots][limb table][block info][barriers][partial sums][abort flag]
     uint8_t* table = smem + static_cast<size_t>(S) * a.slot_bytes;
-    int* binfo = reinterpret_cast<int*>(table + static_cast<size_t>(nblocks) * kLimbBlockBytes);
+    int* binfo = reinterpret_cast<int*>(table + static_cast<size_t>(table_blocks) * kLimbBlockBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(
-        reinterpret_cast<uint8_t*>(binfo) + ((static_cast<size_t>(nblocks) * 20u + 7u) & ~static_cast<size_t>(7)));
+        reinterpret_cast<uint8_t*>(binfo) + ((static_cast<size_t>(table_blocks) * 20u + 7u) & ~static_cast<size_t>(7)));
     uint64_t* empty = full + S;
     uint64_t* redbar = empty + S;
     float* red = reinterpret_cast<float*>(redbar + S);  // [S][W][16]
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(red + static_cast<size_t>(S) * W * 16u);
 
-    // this CTA's rows: an even split of all rows (to one row), cut into tiles of TILE_ROWS
+    // this CTA's rows: an even split of all rows (to one row), cut into 16-row tiles;
+    // the unit of work is (column chunk c, tile j), chunk-major
     const uint64_t row_begin = a.rows * blockIdx.x / gridDim.x;
     const uint64_t row_end = a.rows * (blockIdx.x + 1) / gridDim.x;
-    const uint32_t my_tiles = static_cast<uint32_t>((row_end - row_begin + TILE_ROWS - 1) / TILE_ROWS);
+    const uint32_t my_tiles = static_cast<uint32_t>((row_end - row_begin + kTileRows - 1) / kTileRows);
+    const uint32_t nchunks = MULTI ? a.chunks : 1u;
+    const uint32_t units = my_tiles * nchunks;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -250,30 +310,37 @@ __global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gem
             mbar_init(&empty[s], W);
             mbar_init(&redbar[s], W);
         }
+        *abort_flag = 0u;
         fence_barrier_init();
     }
     __syncthreads();
 
     if (warp == W) {
-        // ---------------- producer: one bulk copy per row into a padded slot row ----------------
-        // Lane r issues row r of the tile: a single issuing thread is limited to
-        // roughly one bulk copy per 50-80 ns, far below what HBM delivers.
+        // ---------------- producer ----------------
+        // Lane r copies row r's chunk (the whole row when there is one chunk)
+        // into its padded shared-memory row: 16 copies issued in parallel.
         const uint64_t policy = l2_policy_evict_first();
-        uint32_t slot = 0, use = 0, j = 0;
-        for (; j < my_tiles; ++j) {
+        uint32_t slot = 0, use = 0, u = 0;
+        for (; u < units; ++u) {
             bool ok = true;
             if (lane == 0 && use > 0) ok = mbar_wait_bounded(&empty[slot], (use - 1u) & 1u, a.status, 11u);
-            if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
-            const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * TILE_ROWS;
-            const uint64_t left = row_end - row0;
-            const uint32_t nrows = left < TILE_ROWS ? static_cast<uint32_t>(left) : TILE_ROWS;
-            if (lane == 0) mbar_arrive_expect_tx(&full[slot], nrows * a.row_bytes);
-            __syncwarp();
-            if (lane < nrows) {
-                uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes + static_cast<size_t>(lane) * a.row_stride;
-                const uint8_t* src = a.w + (row0 + lane) * a.row_bytes;
-                bulk_copy_g2s(dst, src, a.row_bytes, &full[slot], policy);
+            if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) {
+                if (lane == 0) *abort_flag = 1u;
+                break;
             }
+            const uint32_t c = u / my_tiles, j = u - c * my_tiles;
+            const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * kTileRows;
+            const uint64_t left = row_end - row0;
+            const uint32_t nrows = left < kTileRows ? static_cast<uint32_t>(left) : kTileRows;
+            uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
+            const uint32_t pair0 = c * a.chunk_pairs;
+            const uint32_t cp = a.pairs_total - pair0 < a.chunk_pairs ? a.pairs_total - pair0 : a.chunk_pairs;
+            const uint32_t cbytes = cp * Pair<TYPE>::kBytes, cofs = pair0 * Pair<TYPE>::kBytes;
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], nrows * cbytes);
+            __syncwarp();
+            if (lane < nrows)
+                bulk_copy_g2s(dst + static_cast<size_t>(lane) * a.row_pitch, a.w + (row0 + lane) * a.row_bytes + cofs,
+                              cbytes, &full[slot], policy);
             if (++slot == S) {
                 slot = 0;
                 ++use;
@@ -281,121 +348,112 @@ __global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gem
         }
         // drain: every issued copy must land before the CTA may exit
         if (lane == 0) {
-            const uint32_t first = j > S ? j - S : 0;
-            for (uint32_t k = first; k < j; ++k) mbar_wait_bounded(&full[k % S], (k / S) & 1u, a.status, 12u);
+            const uint32_t first = u > S ? u - S : 0;
+            for (uint32_t k = first; k < u; ++k) mbar_wait_bounded(&full[k % S], (k / S) & 1u, a.status, 12u);
         }
         return;
     }
 
-    // ---------------- consumers: warp w owns block pairs [w*PAIRS, (w+1)*PAIRS) ----------------
-    grid_dependency_wait();  // x may come from the previous kernel
-    build_limb_table<TYPE == kQ4_0>(a.x, nblocks, threadIdx.x, W * 32u, table, binfo);
-    named_barrier_sync(1, W * 32u);
+    // ---------------- consumers: warp w owns block pairs [w*PAIRS, (w+1)*PAIRS) of each chunk ----------------
     constexpr bool kQ4 = TYPE == kQ4_0;
-    XPair xs[PAIRS];
-#pragma unroll
-    for (uint32_t p = 0; p < PAIRS; ++p) xs[p] = load_xpair(table, binfo, warp * PAIRS + p, lane, kQ4);
-    grid_launch_dependents();
-
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;  // this lane's D block within a pair
     const size_t col0 = static_cast<size_t>(warp) * PAIRS * Pair<TYPE>::kBytes;
-    uint32_t slot = 0, parity = 0;
-    for (uint32_t j = 0; j < my_tiles; ++j) {
-        if (!mbar_wait_bounded(&full[slot], parity, a.status, 13u)) break;
-        const uint8_t* tile = smem + static_cast<size_t>(slot) * a.slot_bytes;
-        const uint8_t* r0p = tile + static_cast<size_t>(g) * a.row_stride + col0;
-        const uint8_t* r1p = r0p + static_cast<size_t>(8) * a.row_stride;
-        float acc0 = 0.f, acc1 = 0.f;
+    // fragment rows g and g+8 = tile rows g and g+8
+    const size_t off_a = static_cast<size_t>(g) * a.row_pitch + col0;
+    const size_t off_b = off_a + 8u * static_cast<size_t>(a.row_pitch);
+
+    grid_dependency_wait();  // x may come from the previous kernel
+    bool ok = true;
+    uint32_t slot = 0, parity = 0, u = 0;
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        const uint32_t pair0 = c * a.chunk_pairs;
+        const uint32_t cp = a.pairs_total - pair0 < a.chunk_pairs ? a.pairs_total - pair0 : a.chunk_pairs;
+        if (c > 0) named_barrier_sync(1, W * 32u);  // every warp has its x registers of chunk c-1
+        build_limb_table<kQ4>(a.x + static_cast<size_t>(pair0) * 64u, 2u * cp, threadIdx.x, W * 32u, table, binfo);
+        named_barrier_sync(1, W * 32u);
+        const uint32_t pw = warp * PAIRS;
+        const uint32_t valid = cp > pw ? (cp - pw < PAIRS ? cp - pw : PAIRS) : 0u;  // warp-uniform
+        XPair xs[PAIRS];
 #pragma unroll
         for (uint32_t p = 0; p < PAIRS; ++p) {
-            const uint8_t* p0 = r0p + p * Pair<TYPE>::kBytes;
-            const uint8_t* p1 = r1p + p * Pair<TYPE>::kBytes;
-            int d[4];
-            if constexpr (TYPE == kQ8_0) {
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {
-                    // even block: quant bytes 16h+4t.. at pair offset 2+16h+4t (2 mod 4)
-                    const uint32_t o = 16u * h + 4u * t;
-                    const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + o);
-                    const uint32_t a0 = __funnelshift_r(e0[0], e0[1], 16);
-                    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
-                    uint32_t a1 = 0, a3 = 0;
-                    if (TILE_ROWS == 16) {
-                        const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + o);
-                        a1 = __funnelshift_r(e1[0], e1[1], 16);
-                        a3 = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
-                    }
-                    imma(d, a0, a1, a2, a3, xs[p].b0[h], xs[p].b1[h], h == 0, false);
-                }
+            if (p < valid) {
+                xs[p] = load_xpair(table, binfo, pw + p, lane, kQ4);
             } else {
-                // even block quant bytes 4t.. at pair offset 2+4t; odd block at 20+4t
-                const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + 4u * t);
-                const uint32_t w0 = __funnelshift_r(e0[0], e0[1], 16);
-                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(p0 + 20u + 4u * t);
-                uint32_t w1 = 0, w3 = 0;
-                if (TILE_ROWS == 16) {
-                    const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + 4u * t);
-                    w1 = __funnelshift_r(e1[0], e1[1], 16);
-                    w3 = *reinterpret_cast<const uint32_t*>(p1 + 20u + 4u * t);
+                xs[p].b0[0] = xs[p].b0[1] = xs[p].b1[0] = xs[p].b1[1] = 0u;
+                xs[p].scale = 0.f;
+                xs[p].offset = 0;
+            }
+        }
+        if (c == 0) grid_launch_dependents();
+
+        for (uint32_t j = 0; j < my_tiles; ++j, ++u) {
+            if (ok && *abort_flag != 0u) ok = false;
+            if (ok && !mbar_wait_bounded(&full[slot], parity, a.status, 13u)) {
+                ok = false;
+                *abort_flag = 1u;
+            }
+            if (ok) {
+                const uint8_t* tile = smem + static_cast<size_t>(slot) * a.slot_bytes;
+                const uint8_t* r0p = tile + off_a;
+                const uint8_t* r1p = tile + off_b;
+                float acc0 = 0.f, acc1 = 0.f;
+                if (valid == PAIRS)  // every pair of the slice exists: no per-pair checks
+                    tile_dot<TYPE, PAIRS, false>(r0p, r1p, xs, valid, t, scale_blk, acc0, acc1);
+                else
+                    tile_dot<TYPE, PAIRS, true>(r0p, r1p, xs, valid, t, scale_blk, acc0, acc1);
+                // fold the four t-lanes (columns) of each row
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+                float* rs = red + (static_cast<size_t>(slot) * W + warp) * 16u;
+                if (t == 0) {
+                    rs[g] = acc0;
+                    rs[g + 8] = acc1;
                 }
-                const uint32_t m = 0x0F0F0F0Fu;
-                imma(d, w0 & m, w1 & m, w2 & m, w3 & m, xs[p].b0[0], xs[p].b1[0], true, true);
-                imma(d, (w0 >> 4) & m, (w1 >> 4) & m, (w2 >> 4) & m, (w3 >> 4) & m, xs[p].b0[1], xs[p].b1[1], false,
-                     true);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&redbar[slot]);
+                if (warp != 0) {
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                } else {
+                    // warp 0 folds the column slices of every row in fixed order; chunks
+                    // add up in y in chunk order (only this thread touches the row)
+                    if (!mbar_wait_bounded(&redbar[slot], parity, a.status, 14u)) {
+                        ok = false;
+                        *abort_flag = 1u;
+                    } else {
+                        const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * kTileRows;
+                        if (lane < kTileRows && row0 + lane < row_end) {
+                            const float* rr = red + static_cast<size_t>(slot) * W * 16u + lane;
+                            float v = 0.f;
+                            for (uint32_t k = 0; k < W; ++k) v += rr[k * 16u];
+                            if (!MULTI || c == 0)
+                                a.y[row0 + lane] = v;
+                            else
+                                a.y[row0 + lane] += v;
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[slot]);
+                    }
+                }
             }
-            // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
-            const int v0 = d[0] * 128 + d[1] - xs[p].offset;
-            const float s0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk)) * xs[p].scale;
-            acc0 = fmaf(static_cast<float>(v0), s0, acc0);
-            if (TILE_ROWS == 16) {
-                const int v1 = d[2] * 128 + d[3] - xs[p].offset;
-                const float s1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk)) * xs[p].scale;
-                acc1 = fmaf(static_cast<float>(v1), s1, acc1);
+            if (++slot == S) {
+                slot = 0;
+                parity ^= 1u;
             }
-        }
-        // fold the four t-lanes (columns) of each row
-        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
-        acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
-        acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
-        float* rs = red + (static_cast<size_t>(slot) * W + warp) * 16u;
-        if (t == 0) {
-            rs[g] = acc0;
-            rs[g + 8] = acc1;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&redbar[slot]);
-        if (warp != 0) {
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        } else {
-            // warp 0 folds the column slices of every row in fixed order
-            if (!mbar_wait_bounded(&redbar[slot], parity, a.status, 14u)) break;
-            const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * TILE_ROWS;
-            if (lane < TILE_ROWS && row0 + lane < row_end) {
-                const float* rr = red + static_cast<size_t>(slot) * W * 16u + lane;
-                float v = 0.f;
-                for (uint32_t k = 0; k < W; ++k) v += rr[k * 16u];
-                a.y[row0 + lane] = v;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        if (++slot == S) {
-            slot = 0;
-            parity ^= 1u;
         }
     }
 }
 
-template <uint32_t TYPE, uint32_t TILE_ROWS, uint32_t PAIRS>
+template <uint32_t TYPE, uint32_t PAIRS, bool MULTI>
 cudaError_t launch_imma_t(const ImmaPlan& plan, const ImmaArgs& args, cudaStream_t stream, bool pdl) {
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_imma_kernel<TYPE, TILE_ROWS, PAIRS>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(gemv_imma_kernel<TYPE, PAIRS, MULTI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -409,15 +467,18 @@ cudaError_t launch_imma_t(const ImmaPlan& plan, const ImmaArgs& args, cudaStream
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, TILE_ROWS, PAIRS>, args);
+    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, PAIRS, MULTI>, args);
 }
 
-template <uint32_t TYPE, uint32_t TILE_ROWS>
+template <uint32_t TYPE>
 cudaError_t launch_imma_p(const ImmaPlan& plan, const ImmaArgs& args, cudaStream_t stream, bool pdl) {
     switch (plan.pairs) {
-        case 2: return launch_imma_t<TYPE, TILE_ROWS, 2>(plan, args, stream, pdl);
-        case 4: return launch_imma_t<TYPE, TILE_ROWS, 4>(plan, args, stream, pdl);
-        case 8: return launch_imma_t<TYPE, TILE_ROWS, 8>(plan, args, stream, pdl);
+        case 2: return plan.chunks > 1 ? launch_imma_t<TYPE, 2, true>(plan, args, stream, pdl)
+                                       : launch_imma_t<TYPE, 2, false>(plan, args, stream, pdl);
+        case 4: return plan.chunks > 1 ? launch_imma_t<TYPE, 4, true>(plan, args, stream, pdl)
+                                       : launch_imma_t<TYPE, 4, false>(plan, args, stream, pdl);
+        case 8: return plan.chunks > 1 ? launch_imma_t<TYPE, 8, true>(plan, args, stream, pdl)
+                                       : launch_imma_t<TYPE, 8, false>(plan, args, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -430,55 +491,98 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
                    const ImmaTuning* tune) {
     ImmaPlan p;
     if (type != kQ8_0 && type != kQ4_0) return p;
-    if (cols % 64u || rows == 0 || rows > 0xFFFFFFFFull) return p;
+    if (cols % 64u || cols > 0xFFFFFFFFull || rows == 0 || rows > 0xFFFFFFFFull || num_sms <= 0) return p;
     const uint64_t rb = row_bytes_of(type, cols);
     if (rb % 16u) return p;
+    const uint64_t pair_bytes = type == kQ8_0 ? 68u : 36u;
     const uint64_t pairs_total = cols / 64u;
     const ImmaTuning t = tune ? *tune : ImmaTuning{};
-    // pairs per warp in {8, 4, 2}: the most pairs per warp (more independent
-    // IMMA chains per warp) that still leaves at least 4 consumer warps; 8
-    // pairs allow 15 warps, fewer pairs 16
-    uint32_t pairs = 0, warps = 0;
-    for (uint32_t pp : {8u, 4u, 2u}) {
-        if (pairs_total % pp) continue;
-        const uint64_t w = pairs_total / pp;
-        if (w > (pp >= 8 ? 15u : kImmaMaxWarps)) continue;
-        if (t.warps && w != t.warps) continue;
-        if (warps == 0 || (warps < 4 && w > warps)) {
-            pairs = pp;
-            warps = static_cast<uint32_t>(w);
-        }
-    }
-    if (warps == 0) return p;
-    const uint32_t tile_rows = t.tile_rows ? t.tile_rows : 16u;
-    if (tile_rows != 8 && tile_rows != 16) return p;
-    // padded row pitch: 16 mod 32 bytes keeps the 8 fragment rows in distinct banks
-    const uint64_t stride = (rb % 32u == 16u) ? rb : rb + 16u;
-    const uint64_t tiles = (rows + tile_rows - 1) / tile_rows;
-    const uint64_t slot_bytes = align_up64(tile_rows * stride, 128);
-    const uint64_t nblocks = cols / 32u;
-    const uint64_t fixed = nblocks * kLimbBlockBytes + align_up64(nblocks * 20u, 8);
+    // Column chunks: at most 15 warps x 8 pairs of x limbs live in registers at a
+    // time.  Longer rows are cut into chunks of a multiple of 4 pairs (so every
+    // chunk starts on a 16-byte boundary), streamed one after the other; more
+    // chunks than that minimum when a chunk's 16-row tile would leave fewer than
+    // 3 ring slots.
+    constexpr uint64_t kMaxChunkPairs = 15u * 8u;
     uint64_t budget = t.smem_budget ? t.smem_budget : static_cast<uint64_t>(max_smem_optin);
     if (budget > static_cast<uint64_t>(max_smem_optin)) budget = max_smem_optin;
-    auto smem_of = [&](uint32_t s) { return s * slot_bytes + fixed + 24u * s + 4ull * s * warps * 16u; };
-    // enough slots to hold a CTA's whole row range when it fits, else the most that fit (>= 2)
     const uint32_t grid = static_cast<uint32_t>(rows < static_cast<uint64_t>(num_sms) ? rows : num_sms);
     const uint64_t rows_per_cta = (rows + grid - 1) / grid;
-    uint32_t slots = t.slots ? t.slots : static_cast<uint32_t>((rows_per_cta + tile_rows - 1) / tile_rows);
-    if (slots < 2) slots = 2;
-    if (slots > 8) slots = 8;
-    while (slots > 2 && smem_of(slots) > budget) --slots;
-    if (smem_of(slots) > budget) return p;
+    const uint64_t tiles_per_cta = (rows_per_cta + kTileRows - 1) / kTileRows;
+
+    struct Cand {
+        bool ok = false;
+        uint64_t chunks = 0, chunk_pairs = 0, pitch = 0, slot_bytes = 0, slots = 0, smem = 0;
+        uint32_t pairs = 0, warps = 0;
+    };
+    auto evaluate = [&](uint64_t chunks) {
+        Cand c;
+        uint64_t cpairs = pairs_total;
+        if (chunks > 1) {
+            if (pairs_total % 4u) return c;
+            cpairs = align_up64((pairs_total + chunks - 1) / chunks, 4);
+            if ((pairs_total + cpairs - 1) / cpairs != chunks) return c;
+        }
+        if (cpairs > kMaxChunkPairs) return c;
+        // pairs per warp in {8, 4, 2}: the most pairs per warp (more independent
+        // IMMA chains per warp) that still leaves at least 8 consumer warps, else
+        // the most warps; 8 pairs allow 15 warps, fewer pairs 16.  The last warp
+        // may own fewer pairs.
+        for (uint32_t pp : {8u, 4u, 2u}) {
+            const uint64_t w = (cpairs + pp - 1) / pp;
+            if (w > (pp >= 8 ? 15u : kImmaMaxWarps)) continue;
+            if (t.warps && w != t.warps) continue;
+            if (c.warps == 0 || (c.warps < 8 && w > c.warps)) {
+                c.pairs = pp;
+                c.warps = static_cast<uint32_t>(w);
+            }
+        }
+        if (c.warps == 0) return c;
+        // one bulk copy per tile row (its chunk) into a row of pitch 16 mod 32
+        // bytes, so the eight fragment rows of a load sit in distinct banks
+        // (copying two rows per copy into 2-row groups measured no faster)
+        const uint64_t cbytes = cpairs * pair_bytes;
+        c.pitch = (cbytes % 32u == 16u) ? cbytes : cbytes + 16u;
+        c.slot_bytes = align_up64(kTileRows * c.pitch, 128);
+        const uint64_t table_blocks = 2u * cpairs;
+        const uint64_t fixed = table_blocks * kLimbBlockBytes + align_up64(table_blocks * 20u, 8) + 16u;
+        auto smem_of = [&](uint64_t s) { return s * c.slot_bytes + fixed + 24u * s + 4ull * s * c.warps * 16u; };
+        // enough slots to hold a CTA's whole work when it fits, else the most that fit (>= 2)
+        uint64_t slots = t.slots ? t.slots : tiles_per_cta * chunks;
+        if (slots < 2) slots = 2;
+        if (slots > 8) slots = 8;
+        while (slots > 2 && smem_of(slots) > budget) --slots;
+        if (smem_of(slots) > budget) return c;
+        c.chunks = chunks;
+        c.chunk_pairs = cpairs;
+        c.slots = slots;
+        c.smem = smem_of(slots);
+        c.ok = true;
+        return c;
+    };
+    const uint64_t c_min = (pairs_total + kMaxChunkPairs - 1) / kMaxChunkPairs;
+    Cand best;
+    for (uint64_t chunks = c_min; chunks <= c_min + 8 && chunks <= pairs_total; ++chunks) {
+        const Cand c = evaluate(chunks);
+        if (!c.ok) continue;
+        if (!best.ok || (best.slots < 3 && c.slots > best.slots)) best = c;
+        if (best.slots >= 3 || best.slots >= tiles_per_cta * best.chunks) break;
+    }
+    if (!best.ok) return p;
+    const uint64_t chunks = best.chunks, chunk_pairs = best.chunk_pairs, pitch = best.pitch;
+    const uint64_t slots = best.slots, slot_bytes = best.slot_bytes;
+    const uint32_t pairs = best.pairs, warps = best.warps;
     p.type = type;
     p.warps = warps;
     p.pairs = pairs;
-    p.tile_rows = tile_rows;
-    p.row_stride = static_cast<uint32_t>(stride);
-    p.tiles = static_cast<uint32_t>(tiles);
-    p.slots = slots;
+    p.tile_rows = kTileRows;
+    p.row_stride = static_cast<uint32_t>(pitch);
+    p.tiles = static_cast<uint32_t>((rows + kTileRows - 1) / kTileRows);
+    p.slots = static_cast<uint32_t>(slots);
     p.slot_bytes = static_cast<uint32_t>(slot_bytes);
     p.grid = grid;
-    p.smem_bytes = static_cast<uint32_t>(smem_of(slots));
+    p.smem_bytes = static_cast<uint32_t>(best.smem);
+    p.chunks = static_cast<uint32_t>(chunks);
+    p.chunk_pairs = static_cast<uint32_t>(chunk_pairs);
     p.ok = true;
     return p;
 }
@@ -490,20 +594,17 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
     a.x = x;
     a.y = y;
     a.rows = rows;
-    a.cols = static_cast<uint32_t>(cols);
     a.row_bytes = static_cast<uint32_t>(row_bytes_of(plan.type, cols));
-    a.row_stride = plan.row_stride;
-    a.tiles = plan.tiles;
+    a.pairs_total = static_cast<uint32_t>(cols / 64u);
+    a.chunk_pairs = plan.chunk_pairs;
+    a.chunks = plan.chunks;
+    a.row_pitch = plan.row_stride;
     a.warps = plan.warps;
     a.slots = plan.slots;
     a.slot_bytes = plan.slot_bytes;
     a.status = status;
-    if (plan.type == kQ8_0) {
-        return plan.tile_rows == 16 ? launch_imma_p<kQ8_0, 16>(plan, a, stream, pdl)
-                                    : launch_imma_p<kQ8_0, 8>(plan, a, stream, pdl);
-    }
-    return plan.tile_rows == 16 ? launch_imma_p<kQ4_0, 16>(plan, a, stream, pdl)
-                                : launch_imma_p<kQ4_0, 8>(plan, a, stream, pdl);
+    if (plan.type == kQ8_0) return launch_imma_p<kQ8_0>(plan, a, stream, pdl);
+    return launch_imma_p<kQ4_0>(plan, a, stream, pdl);
 }
 
 }  // namespace nedo_gpu

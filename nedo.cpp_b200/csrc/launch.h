@@ -54,26 +54,27 @@ cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, 
                           cudaStream_t stream, bool pdl);
 
 // Batch-1 Q8_0 / Q4_0 on the int8 tensor pipe (mma.sync m16n8k32, x as exact
-// int8 limbs).  Row tiles of 8 or 16 rows, each warp a fixed column slice.
+// int8 limbs).  16-row tiles, each warp a fixed column slice of a column
+// chunk; rows longer than one chunk are streamed chunk after chunk.
 struct ImmaPlan {
     bool ok = false;
     uint32_t type = 0;
-    uint32_t warps = 0;       // consumer warps (column slices); one more warp streams tiles
-    uint32_t pairs = 0;       // block pairs per warp
-    uint32_t tile_rows = 0;
-    uint32_t row_stride = 0;  // padded shared-memory row pitch
+    uint32_t warps = 0;        // consumer warps (column slices); one more warp streams tiles
+    uint32_t pairs = 0;        // block pairs per warp
+    uint32_t tile_rows = 0;    // 16
+    uint32_t row_stride = 0;   // shared-memory pitch of one tile row (16 mod 32 bytes)
     uint32_t tiles = 0;
     uint32_t slots = 0;
     uint32_t slot_bytes = 0;
     uint32_t smem_bytes = 0;
     uint32_t grid = 0;
+    uint32_t chunks = 0;       // column chunks per row
+    uint32_t chunk_pairs = 0;  // block pairs per chunk
 };
 
 struct ImmaTuning {
     uint32_t warps = 0;
-    uint32_t tile_rows = 0;
     uint32_t slots = 0;
-    uint32_t piece_bytes = 0;
     uint32_t smem_budget = 0;
 };
 
