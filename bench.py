@@ -17,7 +17,8 @@ Workloads (default q4_0_11008x4096):
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max over
-ranks.  At N=1 the K steps run as one CUDA graph.  Weight copies rotate so the
+ranks.  The K steps run as one CUDA graph (at N>1 with the NCCL all-gather of
+each step inside it).  Weight copies rotate so the
 rotating set exceeds 4x L2 (each step reads a weight that is not in L2).
 
 `e2e` repeats the metric through the host entry point of the C ABI
@@ -248,6 +249,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     import torch.distributed as dist
 
     import nedo_gpu
+    from nedo_gpu.shard import ShardedMatvec
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -278,10 +280,14 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         else:
             lib.matvec_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), 1, s)
 
+    # N > 1: this rank's rows, then the NCCL all-gather of the y slices
+    sm = ShardedMatvec(t, rows_total, cols) if world > 1 else None
+
     def step(k):
-        launch(k, stream.cuda_stream)
-        if world > 1:
-            dist.all_gather_into_tensor(y_full, y)
+        if sm is None:
+            launch(k, stream.cuda_stream)
+        else:
+            sm.run(lambda xv, yl: launch(k, stream.cuda_stream), x, y, y_full)
 
     def barrier():
         if world > 1:
@@ -308,6 +314,17 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
             launch(k, torch.cuda.current_stream().cuda_stream)
     graph.replay()
     torch.cuda.synchronize()
+    # N > 1: the whole step (matvec + NCCL all-gather) as one graph of K steps;
+    # every rank captures the same collectives in the same order
+    step_graph = None
+    if world > 1:
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(step_graph, stream=stream):
+            for k in range(args.steps):
+                step(k)
+        step_graph.replay()
+        torch.cuda.synchronize()
+        barrier()
 
     sampler = ClockSampler(local_rank)
     sampler.start()
@@ -324,8 +341,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         if world == 1:
             graph.replay()
         else:
-            for k in range(args.steps):
-                step(k)
+            step_graph.replay()
         ev1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -343,6 +359,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     kernel_ms = max_over_ranks(k0.elapsed_time(k1)) / args.steps
     lib.status(stream.cuda_stream)
     del graph
+    del step_graph  # holds NCCL calls: released before the process group goes
 
     bytes_total = algorithmic_bytes(t, rows_total, cols)  # whole job, all ranks
     ms_per_step = region_ms / args.steps
@@ -364,7 +381,8 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
         "config": dict(workload_config(args.workload, wl, world),
                        l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
-                          f"> 4x L2)", graph="K steps captured as one CUDA graph" if world == 1 else "eager",
+                          f"> 4x L2)", graph="K steps (matvec" + (" + NCCL all-gather" if world > 1 else "")
+                          + ") captured as one CUDA graph",
                        pdl=True, plan=plan),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -407,12 +425,15 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
     y = torch.empty(rows, dtype=torch.float32, device=device)
     y_full = torch.empty(rows_total, dtype=torch.float32, device=device)
 
+    from nedo_gpu.shard import ShardedMatvec
+
+    sm = ShardedMatvec(t, rows_total, cols)
+
     def one(k):
         with torch.cuda.stream(stream):
             xd.copy_(x_pin, non_blocking=True)
-            lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xd.data_ptr(), y.data_ptr(), 1,
-                           stream.cuda_stream)
-            dist.all_gather_into_tensor(y_full, y)
+            sm.run(lambda xv, yl: lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xv.data_ptr(),
+                                                 yl.data_ptr(), 1, stream.cuda_stream), xd, y, y_full)
             y_pin.copy_(y_full, non_blocking=True)
         stream.synchronize()
 
