@@ -14,6 +14,10 @@ Workloads (default q4_0_11008x4096):
   f16_head_128000x2048 F16 128000x2048 LM-head matvec with the argmax fused.
   q4_0_32768x32768     Q4_0 32768x32768, row-sharded over N GPUs + NCCL all-gather
                        of y: strong scaling (fixed total matrix).
+  q8_0_prefill_512x4096x14336
+                       prompt-shaped batch: 512 token vectors through one Q8_0
+                       14336x4096 weight (the tcgen05 GEMM), TFLOP/s; replicas
+                       at N > 1.
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max over
@@ -48,12 +52,15 @@ from nedo_gpu import blocks as B  # noqa: E402
 METRIC = "Q8_0/Q4_0/F16 matvec HBM GB/s & % of B200 peak; prefill GEMM TFLOP/s @1-8 GPU"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 WORKLOADS = {
     "q4_0_11008x4096": dict(type=B.Q4_0, rows=11008, cols=4096, shard="weak", argmax=False),
     "q8_0_4096x4096": dict(type=B.Q8_0, rows=4096, cols=4096, shard="weak", argmax=False),
     "f16_head_128000x2048": dict(type=B.F16, rows=128000, cols=2048, shard="weak", argmax=True),
     "q4_0_32768x32768": dict(type=B.Q4_0, rows=32768, cols=32768, shard="strong", argmax=False),
+    "q8_0_prefill_512x4096x14336": dict(type=B.Q8_0, rows=14336, cols=4096, shard="replica", argmax=False,
+                                        batch=512),
 }
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures
@@ -69,14 +76,18 @@ def env_int(name, default):
     return int(v) if v not in (None, "") else default
 
 
-def peaks():
+def peaks(tensor=False):
+    """(peak, source): HBM GB/s, or dense bf16 TFLOP/s (burst: the kernel is timed
+    in isolation) for tensor-core workloads."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    key = "bf16_tflops" if tensor else "hbm_gbs"
     try:
         with open(path) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p[key]), f"measured (MEASURED_PEAKS.json {key})"
     except (OSError, KeyError, ValueError):
-        return FALLBACK_HBM_GBS, "fallback"
+        return (FALLBACK_BF16_TFLOPS, "fallback 1.59 PFLOP/s") if tensor else (FALLBACK_HBM_GBS,
+                                                                                "fallback 6.65 TB/s")
 
 
 def host_cores():
@@ -87,7 +98,7 @@ def host_cores():
 
 
 def shard_rows(wl, world):
-    if wl["shard"] == "weak":
+    if wl["shard"] in ("weak", "replica"):
         return wl["rows"], wl["rows"] * world
     assert wl["rows"] % world == 0
     return wl["rows"] // world, wl["rows"]
@@ -96,6 +107,18 @@ def shard_rows(wl, world):
 def algorithmic_bytes(type_, rows, cols):
     """W + x + y of one matvec (GGUF block bytes)."""
     return rows * B.row_bytes(type_, cols) + 4 * cols + 4 * rows
+
+
+def batch_of(wl):
+    return wl.get("batch", 1)
+
+
+def work_of(wl, rows_total, batch=None):
+    """(units, unit name, scale) of one step: bytes for matvecs, FLOPs for batches."""
+    b = batch_of(wl) if batch is None else batch
+    if batch_of(wl) > 1:
+        return 2.0 * b * rows_total * wl["cols"], "TFLOP/s", 1e12
+    return float(algorithmic_bytes(wl["type"], rows_total, wl["cols"])), "GB/s", 1e9
 
 
 # ------------------------------------------------------------------ clocks
@@ -150,20 +173,25 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_reference(type_, rows, cols, seed):
-    """(callable, kind, cores) running the reference CPU kernel on one matrix."""
+# The reference processes a prompt as one matvec per token (src/model.cpp:262-266);
+# a batch workload's CPU sample is this many of them per call.
+CPU_BATCH_SAMPLE = 8
+
+
+def cpu_reference(type_, rows, cols, seed, nvec=1):
+    """(callable, kind, cores) running the reference CPU kernel: `nvec` matvecs over one matrix."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
     w = B.gen_weight(type_, rows, cols, seed)
-    x = B.gen_x(cols, seed)
+    xs = [B.gen_x(cols, seed + k) for k in range(nvec)]
     if O.Reference.available():
         ref = O.Reference()
         cores = host_cores()
         ref.set_threads(cores)
-        return (lambda: ref.matvec(type_, rows, cols, w, x)), "reference", cores
+        return (lambda: [ref.matvec(type_, rows, cols, w, x) for x in xs]), "reference", cores
     orc = O.Oracle()
-    return (lambda: orc.matvec(type_, rows, cols, w, x)), "port", 1
+    return (lambda: [orc.matvec(type_, rows, cols, w, x) for x in xs]), "port", 1
 
 
 def time_cpu(fn, budget_s, max_calls):
@@ -176,35 +204,41 @@ def time_cpu(fn, budget_s, max_calls):
 
 
 def cpu_baseline(wl, rows_total, budget_s=10.0):
-    fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7)
+    nvec = CPU_BATCH_SAMPLE if batch_of(wl) > 1 else 1
+    fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7, nvec=nvec)
     sec, n = time_cpu(fn, budget_s, 100000)
-    gbs = algorithmic_bytes(wl["type"], rows_total, wl["cols"]) / sec / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{n} full {B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} matvecs "
-                      f"({sec * 1e3:.3f} ms each, {n * sec:.1f} s)"}
+    units, unit, scale = work_of(wl, rows_total, batch=nvec)
+    what = f"{B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} matvecs"
+    if nvec > 1:
+        what = f"{nvec}-token samples of the {batch_of(wl)}-token batch ({what}, one per token)"
+    return {"value": round(units / sec / scale, 4), "unit": unit, "cores": cores, "kind": kind,
+            "sample": f"{n} x {what} ({sec * 1e3:.3f} ms each, {n * sec:.1f} s)"}
 
 
 def run_reference_arm(args, wl, world, rank):
     if rank != 0:
         return
     _, rows_total = shard_rows(wl, world)
-    fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7)
+    nvec = CPU_BATCH_SAMPLE if batch_of(wl) > 1 else 1
+    fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7, nvec=nvec)
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         fn()
     sec = (time.perf_counter() - t0) / args.steps
-    gbs = algorithmic_bytes(wl["type"], rows_total, wl["cols"]) / sec / 1e9
+    units, unit, scale = work_of(wl, rows_total, batch=nvec)
+    gbs = units / sec / scale
     line = {
-        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+        "metric": METRIC, "value": round(gbs, 4), "unit": unit, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak" if wl["shard"] == "weak" else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded GGUF blocks)",
         "config": workload_config(args.workload, wl, world),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-                         "sample": f"each step one full {B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} matvec"},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": unit, "cores": cores, "kind": kind,
+                         "sample": f"each step {nvec} full {B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} "
+                                   f"matvec{'s (a sample of the batch, one per token)' if nvec > 1 else ''}"},
+        "e2e": {"value": round(gbs, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -212,13 +246,19 @@ def run_reference_arm(args, wl, world, rank):
 def workload_config(name, wl, world):
     rows, rows_total = shard_rows(wl, world)
     t = B.TYPE_NAMES[wl["type"]]
-    desc = f"{t} matvec {rows_total}x{wl['cols']} batch 1"
-    if world > 1:
+    desc = f"{t} matvec {rows_total}x{wl['cols']} batch {batch_of(wl)}"
+    if batch_of(wl) > 1:
+        desc = (f"{t} {wl['rows']}x{wl['cols']} weight x {batch_of(wl)} token vectors "
+                f"(prefill GEMM, M={batch_of(wl)} K={wl['cols']} N={wl['rows']})")
+        if world > 1:
+            desc += f", {world} independent replicas"
+    elif world > 1:
         desc += f", row-sharded {rows} rows per GPU + NCCL all-gather of y"
     if wl["argmax"]:
         desc += ", argmax fused"
     return {"workload": name, "description": desc, "type": t, "rows_total": rows_total, "rows_per_gpu": rows,
-            "cols": wl["cols"], "batch": 1, "parallelism": f"rowshard{world}" if world > 1 else "single"}
+            "cols": wl["cols"], "batch": batch_of(wl),
+            "parallelism": ("replicas" if wl["shard"] == "replica" else f"rowshard{world}") if world > 1 else "single"}
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -265,23 +305,25 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     w = make_weights(torch, t, rows, cols, copies, seed=1000 + rank, device=device)
     gx = torch.Generator(device=device)
     gx.manual_seed(7)
-    x = torch.randn(cols, generator=gx, device=device, dtype=torch.float32)
-    y = torch.empty(rows, dtype=torch.float32, device=device)
-    y_full = torch.empty(rows_total, dtype=torch.float32, device=device) if world > 1 else y
+    nb = batch_of(wl)
+    x = torch.randn((nb, cols) if nb > 1 else cols, generator=gx, device=device, dtype=torch.float32)
+    y = torch.empty((nb, rows) if nb > 1 else rows, dtype=torch.float32, device=device)
+    y_full = torch.empty(rows_total, dtype=torch.float32, device=device) if world > 1 and nb == 1 else y
     idx = torch.zeros(1, dtype=torch.int64, device=device)
     val = torch.zeros(1, dtype=torch.float32, device=device)
     stream = torch.cuda.Stream(device=device)
-    plan = lib.plan_info(t, rows, cols)
+    plan = lib.plan_info(t, rows, cols, nb)
 
     def launch(k, s):
         wp = w[k % copies].data_ptr()
         if wl["argmax"]:
             lib.matvec_argmax_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), idx.data_ptr(), val.data_ptr(), s)
         else:
-            lib.matvec_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), 1, s)
+            lib.matvec_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), nb, s)
 
     # N > 1: this rank's rows, then the NCCL all-gather of the y slices
-    sm = ShardedMatvec(t, rows_total, cols) if world > 1 else None
+    # (replica workloads run independently on every GPU: no collective)
+    sm = ShardedMatvec(t, rows_total, cols) if world > 1 and wl["shard"] != "replica" else None
 
     def step(k):
         if sm is None:
@@ -361,36 +403,38 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     del graph
     del step_graph  # holds NCCL calls: released before the process group goes
 
-    bytes_total = algorithmic_bytes(t, rows_total, cols)  # whole job, all ranks
+    units_total, unit, scale = work_of(wl, rows_total)  # whole job, all ranks
     ms_per_step = region_ms / args.steps
-    value = bytes_total / (ms_per_step * 1e-3) / 1e9
+    value = units_total / (ms_per_step * 1e-3) / scale
 
     # ---- end to end through the C ABI host entry point
     e2e = e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream)
 
-    peak, peak_kind = peaks()
-    per_launch = algorithmic_bytes(t, rows, cols)
-    achieved = per_launch / (kernel_ms * 1e-3) / 1e9
+    tensor = nb > 1
+    peak, peak_kind = peaks(tensor)
+    per_launch, _, _ = work_of(wl, rows)
+    achieved = per_launch / (kernel_ms * 1e-3) / scale
     traffic = NCU_TRAFFIC_BYTES.get(args.workload) if world == 1 else None
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-        "scaling": "weak" if wl["shard"] == "weak" else "strong", "vs_baseline": None,
-        # block dots on the int8 tensor pipe (exact int32) for the IMMA plan, fp32 FMA otherwise
-        "dtype": "int8" if plan.get("path") == 4 else "f32",
+        "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None,
+        # block dots on the int8 tensor pipe (exact int32) for the IMMA plan; fp16
+        # operands with fp32 accumulation on tcgen05 for batches; fp32 FMA otherwise
+        "dtype": {4: "int8", 5: "f16"}.get(plan.get("path"), "f32"),
         "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
         "config": dict(workload_config(args.workload, wl, world),
                        l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
                           f"> 4x L2)", graph="K steps (matvec" + (" + NCCL all-gather" if world > 1 else "")
                           + ") captured as one CUDA graph",
                        pdl=True, plan=plan),
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                     else "fallback 6.65 TB/s", "launch_us": round(kernel_ms * 1e3, 3),
-                     "bytes_per_launch": per_launch},
+        "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                     "launch_us": round(kernel_ms * 1e3, 3),
+                     ("flops_per_step" if tensor else "bytes_per_launch"): per_launch},
         "e2e": e2e,
-        "gpu_launches": args.steps,  # one matvec kernel per step (argmax fused into it)
+        # one matvec kernel per step (argmax fused into it); batches: x -> fp16, then the GEMM
+        "gpu_launches": args.steps * (2 if plan.get("path") == 5 else 1),
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -401,6 +445,40 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
 
 def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream):
     t, cols = wl["type"], wl["cols"]
+    nb = batch_of(wl)
+    if nb > 1:
+        # a prompt-sized batch end to end: pinned host x -> device, the batched
+        # matvec (x -> fp16 + tcgen05 GEMM), y -> pinned host, every step
+        x_pin = torch.from_numpy(np.random.default_rng(7).standard_normal((nb, cols), dtype=np.float32)).pin_memory()
+        y_pin = torch.empty((nb, rows), dtype=torch.float32).pin_memory()
+        xd = torch.empty((nb, cols), dtype=torch.float32, device=device)
+        yd = torch.empty((nb, rows), dtype=torch.float32, device=device)
+
+        def one(k):
+            with torch.cuda.stream(stream):
+                xd.copy_(x_pin, non_blocking=True)
+                lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xd.data_ptr(), yd.data_ptr(), nb,
+                               stream.cuda_stream)
+                y_pin.copy_(yd, non_blocking=True)
+            stream.synchronize()
+
+        for k in range(3):
+            one(k)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for k in range(args.steps):
+            one(k)
+        sec = time.perf_counter() - t0
+        if world > 1:
+            tt = torch.tensor([sec], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            sec = float(tt.item())
+        sec /= args.steps
+        units, unit, scale = work_of(wl, rows_total)
+        return {"value": round(units / sec / scale, 2), "unit": unit, "h2d_bytes_per_step": 4 * nb * cols,
+                "d2h_bytes_per_step": 4 * nb * rows,
+                "path": "pinned H2D + nedo_gpu_matvec_dev(batch) + D2H", "ms_per_step": round(sec * 1e3, 4)}
     x_host = np.random.default_rng(7).standard_normal(cols, dtype=np.float32)
     n_host = min(copies, 8) if world == 1 else 1
     if world == 1:

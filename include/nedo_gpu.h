@@ -117,7 +117,9 @@ NEDO_GPU_API int nedo_gpu_cache_clear(void);
  * vectors: y_dev[b][r] = dot(row r, x_dev[b]), b < batch.  batch == 1 is the
  * decode path (src/model.cpp:217-259); batch > 1 replaces `batch` serial
  * calls over the same weight, which is how the reference processes a prompt
- * (src/model.cpp:262-266). */
+ * (src/model.cpp:262-266).  From 16 vectors on, the batch runs as one
+ * tensor-core GEMM with x and the dequantised weight rounded to fp16 (fp32
+ * accumulation); the first such call on a device allocates an fp16 copy of x. */
 NEDO_GPU_API int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
                         float* y_dev, uint32_t batch, void* stream);
 
@@ -155,7 +157,8 @@ NEDO_GPU_API int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_
 NEDO_GPU_API int nedo_gpu_status(void* stream);
 
 /* Describe the kernel choice for a shape: out[0] = path (1 streaming CUDA-core,
- * 2 generic, 3 batched tensor-core, 4 int8 tensor-pipe matvec), out[1] grid,
+ * 2 generic, 3 batched streaming (one launch per vector), 4 int8 tensor-pipe
+ * matvec, 5 tcgen05 GEMM over the batch), out[1] grid,
  * out[2] threads, out[3] dynamic shared bytes, out[4] rows per tile,
  * out[5] ring slots, out[6] slot bytes, out[7] warps per CTA (compute warps for
  * path 4).  n = capacity of out (>= 8). */

@@ -145,4 +145,11 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32
     return d;
 }
 
+// (a & mask) ^ bits as a single LOP3.
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t a, uint32_t mask, uint32_t bits) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(mask), "r"(bits));
+    return d;
+}
+
 }  // namespace nedo_gpu

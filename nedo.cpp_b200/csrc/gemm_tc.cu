@@ -1,0 +1,522 @@
+// gemm_tc.cu -- batched matvec (prefill-shaped GEMM) on the 5th-generation
+// tensor cores: Y[t][r] = sum_k W[r][k] * X[t][k] for a GGUF weight W
+// (rows x cols) and T token vectors X (fp32).
+//
+// The reference has no batched product: a prompt is a loop of single-vector
+// matvecs (src/model.cpp:262-266), each y[r] = dot(row r, x)
+// (src/kernels.cpp:162-169).  Here the tokens become the N dimension of one
+// tcgen05 contraction per 128-row weight tile:
+//
+//   * W stays in GGUF block layout in HBM.  A TMA tensor map over the row bytes
+//     (uint16 elements, so every 256-element chunk of a Q8_0 / Q4_0 row starts on
+//     a 16-byte boundary) brings 128 rows x 256 elements of raw blocks into
+//     shared memory; eight dequant warps turn each block into fp16 d*q (the
+//     product is exact in fp32 and rounded once to fp16) and write the MMA's A
+//     tiles in the 128-byte-swizzled K-major layout.  F16 weights load straight
+//     into that layout with a swizzled tensor map.
+//   * X is converted once to fp16 (round to nearest) and loaded per stage with a
+//     swizzled tensor map as the B operand (tokens x 64 K).
+//   * One thread issues tcgen05.mma kind::f16 (M=128 weight rows, N=256 tokens,
+//     K=16, fp32 accumulators in TMEM); tcgen05.commit releases the stage.
+//   * The dequant warps then read TMEM (tcgen05.ld 32x32b) and store Y.
+//
+// fp16 rounding of x and of d*q is the only difference from the reference's
+// fp32 arithmetic (relative 2^-11 per factor); the products are summed in fp32.
+// Every wait is bounded; TMEM is released on every path.
+#include <cuda.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace nedo_gpu {
+namespace {
+
+constexpr uint32_t kBM = 128;         // weight rows per tile (MMA M, TMEM lanes)
+constexpr uint32_t kBN = 256;         // tokens per tile (MMA N, TMEM columns)
+constexpr uint32_t kBK = 64;          // K per stage: one 128-byte fp16 row of a swizzle atom
+constexpr uint32_t kRawK = 256;       // K per raw weight chunk: 8 GGUF blocks
+// A/B stages: 48 KB each; quantised weights also need two raw chunk slots
+template <uint32_t TYPE>
+constexpr uint32_t stages() {
+    return TYPE == kF16 ? 4u : 3u;
+}
+constexpr uint32_t kRawSlots = 2;
+constexpr uint32_t kDeqWarps = 8;     // warps 2..9: dequant, then epilogue
+constexpr uint32_t kThreads = (2 + kDeqWarps) * 32;
+constexpr uint32_t kStageA = kBM * 128;  // 16 KB
+constexpr uint32_t kStageB = kBN * 128;  // 32 KB
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <uint32_t TYPE>
+struct RawBlock;
+template <>
+struct RawBlock<kQ8_0> {
+    static constexpr uint32_t kBytes = 34;
+};
+template <>
+struct RawBlock<kQ4_0> {
+    static constexpr uint32_t kBytes = 18;
+};
+template <>
+struct RawBlock<kF16> {  // F16 rows load straight into the A tiles (no raw chunk)
+    static constexpr uint32_t kBytes = 64;
+};
+template <uint32_t TYPE>
+constexpr uint32_t raw_row_bytes() {  // bytes of one row of a raw chunk (kRawK elements)
+    return kRawK / 32u * RawBlock<TYPE>::kBytes;
+}
+
+struct GemmArgs {
+    float* y;          // [tokens][ldy]
+    uint32_t rows;     // N of the weight (output features)
+    uint32_t cols;     // K
+    uint32_t tokens;
+    uint32_t ldy;
+    DeviceStatus* status;
+};
+
+// ---- PTX wrappers -------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base + i).
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes (SBO), version 1 (sm_100).  The tile base is 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;            // LBO (unused by swizzled K-major)
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;    // SBO: 8 rows x 128 bytes
+    d |= static_cast<uint64_t>(1u) << 46;            // descriptor version for sm_100
+    d |= static_cast<uint64_t>(2u) << 61;            // SWIZZLE_128B
+    return d;
+}
+
+// kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M x N.
+constexpr uint32_t kIdesc = (1u << 4) | ((kBN >> 3) << 17) | ((kBM >> 4) << 24);
+
+// fp16 tile element (row r, 16-byte chunk c of its 128-byte row) in the
+// 128-byte-swizzled K-major layout: chunk c lands at c ^ (r % 8).
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
+    return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+// Dequantise block BLK (0..7) of row r of a raw chunk into the A stage:
+// elements 32*(BLK%2) .. +32 of the stage's 64-wide K window.  All offsets
+// are compile-time; the block's bytes come from 16-byte aligned loads.
+template <uint32_t TYPE, uint32_t BLK>
+__device__ __forceinline__ void dequant_block(uint32_t raw_row, uint32_t a_stage, uint32_t r) {
+    constexpr uint32_t BB = RawBlock<TYPE>::kBytes;
+    constexpr uint32_t start = BLK * BB;           // block offset in the raw row
+    constexpr uint32_t base = start & ~15u;        // 16-byte aligned window
+    constexpr uint32_t off = start - base;         // 0..14, even
+    constexpr uint32_t nchunks = (off + BB + 15u) / 16u;  // 2 (Q4_0) or 3 (Q8_0)
+    uint32_t w[12];
+#pragma unroll
+    for (uint32_t c = 0; c < 3; ++c) {
+        if (c < nchunks) {
+            const uint4 v = lds128(raw_row + base + 16u * c);
+            w[4 * c] = v.x;
+            w[4 * c + 1] = v.y;
+            w[4 * c + 2] = v.z;
+            w[4 * c + 3] = v.w;
+        } else {
+            w[4 * c] = w[4 * c + 1] = w[4 * c + 2] = w[4 * c + 3] = 0u;
+        }
+    }
+    // byte i of the block is byte (off + i) of the window.  Two quants become an
+    // fp16 pair without int->float conversions: PRMT gathers their bytes into
+    // the low bytes of the two halves, LOP3 puts them under the exponent of
+    // 1024 (fp16 0x6400 + u = 1024 + u, exact for u < 1024), HSUB2 removes the
+    // bias exactly, and HMUL2 by d rounds d*q once (as __float2half_rn(d*q)).
+    // bytes i, i+1 of the block -> bytes 0 and 2 of the result (bytes 1, 3: don't care)
+    auto pair_bytes = [&](uint32_t i) -> uint32_t {
+        const uint32_t k = off + i, wi = k >> 2, bi = k & 3u;
+        // PRMT's 8-byte window: w[wi] = bytes 0..3, w[wi+1] = bytes 4..7
+        return prmt(w[wi], w[wi + 1u < 12u ? wi + 1u : 11u], bi | ((bi + 1u) << 8));
+    };
+    const uint32_t dbits = pair_bytes(0);
+    const __half dh = __ushort_as_half(static_cast<unsigned short>((dbits & 0xFFu) | ((dbits >> 8) & 0xFF00u)));
+    const __half2 d2 = __halves2half2(dh, dh);
+    constexpr uint32_t c_first = (BLK & 1u) * 4u;  // 16-byte chunk index in the 128-byte stage row
+#pragma unroll
+    for (uint32_t c = 0; c < 4; ++c) {  // 8 elements per 16-byte output chunk
+        uint32_t h[4];
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) {
+            const uint32_t el = 8u * c + 2u * e;  // elements el, el+1 of the block
+            __half2 q;
+            if constexpr (TYPE == kQ8_0) {
+                // int8 q: (q ^ 0x80) = q + 128 under the 1024 exponent, minus 1152
+                const uint32_t v = lop_and_xor(pair_bytes(2u + el), 0x00FF00FFu, 0x64806480u);
+                q = __hsub2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1152.0f));
+            } else {
+                // Q4_0: elements j < 16 are the low nibbles of bytes j, elements
+                // j + 16 the high nibbles; value nibble - 8
+                const uint32_t j = el & 15u;
+                uint32_t v = pair_bytes(2u + j);
+                if (el >= 16u) v >>= 4;
+                v = lop_and_or(v, 0x000F000Fu, 0x64006400u);
+                q = __hsub2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1032.0f));
+            }
+            const __half2 p = __hmul2(q, d2);
+            h[e] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        sts128(a_stage + sw128_offset(r, c_first + c), h[0], h[1], h[2], h[3]);
+    }
+}
+
+template <uint32_t I>
+struct Idx {
+    static constexpr uint32_t value = I;
+};
+
+// x (fp32, tokens x cols) -> fp16 (round to nearest), same layout.
+__global__ void x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ xh, uint64_t n) {
+    for (uint64_t i = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) * 4u; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x * 4u) {
+        if (i + 4u <= n) {
+            const float4 v = *reinterpret_cast<const float4*>(x + i);
+            *reinterpret_cast<__half2*>(xh + i) = __floats2half2_rn(v.x, v.y);
+            *reinterpret_cast<__half2*>(xh + i + 2) = __floats2half2_rn(v.z, v.w);
+        } else {
+            for (uint64_t k = i; k < n; ++k) xh[k] = __float2half_rn(x[k]);
+        }
+    }
+}
+
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                   const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned base for the swizzled tiles
+    const uint32_t s0 = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    uint8_t* const sbase = smem_raw + (s0 - smem_addr(smem_raw));
+    constexpr bool kRawW = TYPE != kF16;
+    constexpr uint32_t kS = stages<TYPE>();
+    constexpr uint32_t kRawBytes = kRawW ? kBM * raw_row_bytes<TYPE>() : 0u;
+    const uint32_t sA = s0;                       // kS x 16 KB
+    const uint32_t sB = sA + kS * kStageA;        // kS x 32 KB
+    const uint32_t sRaw = sB + kS * kStageB;          // kRawSlots x raw chunk
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + (sRaw - s0) + kRawSlots * kRawBytes);
+    uint64_t* b_full = bars;                  // [kS] X (and F16 W) tiles landed
+    uint64_t* a_full = bars + kS;        // [kS] A tile written by the dequant warps
+    uint64_t* ab_empty = bars + 2 * kS;  // [kS] MMAs of the stage done
+    uint64_t* raw_full = bars + 3 * kS;  // [kRawSlots]
+    uint64_t* raw_empty = raw_full + kRawSlots;
+    uint64_t* done = raw_empty + kRawSlots;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t row0 = blockIdx.x * kBM;   // weight rows of this tile
+    const uint32_t tok0 = blockIdx.y * kBN;   // tokens of this tile
+    const uint32_t ksteps = (a.cols + kBK - 1) / kBK;
+    const uint32_t chunks = (a.cols + kRawK - 1) / kRawK;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kS; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&a_full[s], kRawW ? kDeqWarps : 1u);
+            mbar_init(&ab_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < kRawSlots; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], kDeqWarps);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM: kBN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kBN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            grid_dependency_wait();  // X may come from the previous kernel
+            uint32_t issued_ks = 0, issued_kc = 0;
+            bool ok = true;
+            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
+                if constexpr (kRawW) {
+                    const uint32_t rs = kc % kRawSlots;
+                    if (kc >= kRawSlots && !mbar_wait_bounded(&raw_empty[rs], ((kc / kRawSlots) - 1u) & 1u, a.status, 31u)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
+                    tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>(kc * (raw_row_bytes<TYPE>() / 2u)),
+                                static_cast<int32_t>(row0), &raw_full[rs]);
+                    issued_kc = kc + 1u;
+                }
+                for (uint32_t j = 0; j < kRawK / kBK; ++j) {
+                    const uint32_t ks = kc * (kRawK / kBK) + j;
+                    if (ks >= ksteps) break;
+                    const uint32_t s = ks % kS;
+                    if (ks >= kS && !mbar_wait_bounded(&ab_empty[s], ((ks / kS) - 1u) & 1u, a.status, 32u)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&b_full[s], kStageB + (kRawW ? 0u : kStageA));
+                    tma_load_2d(sB + s * kStageB, &map_x, static_cast<int32_t>(ks * kBK), static_cast<int32_t>(tok0),
+                                &b_full[s]);
+                    if constexpr (!kRawW)
+                        tma_load_2d(sA + s * kStageA, &map_w, static_cast<int32_t>(ks * kBK),
+                                    static_cast<int32_t>(row0), &b_full[s]);
+                    issued_ks = ks + 1u;
+                }
+            }
+            // drain: the last copies issued into every slot have landed before exit
+            for (uint32_t k = issued_ks > kS ? issued_ks - kS : 0u; k < issued_ks; ++k)
+                mbar_wait_bounded(&b_full[k % kS], (k / kS) & 1u, a.status, 38u);
+            for (uint32_t k = issued_kc > kRawSlots ? issued_kc - kRawSlots : 0u; k < issued_kc; ++k)
+                mbar_wait_bounded(&raw_full[k % kRawSlots], (k / kRawSlots) & 1u, a.status, 39u);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t ks = 0; ks < ksteps && ok; ++ks) {
+                const uint32_t s = ks % kS, ph = (ks / kS) & 1u;
+                ok = mbar_wait_bounded(&b_full[s], ph, a.status, 33u);
+                if constexpr (kRawW) ok = ok && mbar_wait_bounded(&a_full[s], ph, a.status, 34u);
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t ad = sw128_desc(sA + s * kStageA), bd = sw128_desc(sB + s * kStageB);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // K = 16 per MMA: 32 bytes along the row
+                    tc_mma_f16(tmem_d, ad + 2u * kk, bd + 2u * kk, kIdesc, (ks | kk) != 0u);
+                tc_commit(&ab_empty[s]);
+            }
+            tc_commit(done);  // every MMA issued above has completed when this arrives
+        }
+    } else {
+        // ---------------- dequant warps, then epilogue ----------------
+        const uint32_t dt = threadIdx.x - 64u;  // 0..255
+        const uint32_t r = dt & (kBM - 1u);      // tile row
+        const uint32_t half = dt >> 7;           // which block of each stage's pair
+        if constexpr (kRawW) {
+            bool ok = true;
+            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
+                const uint32_t rs = kc % kRawSlots;
+                if (!mbar_wait_bounded(&raw_full[rs], (kc / kRawSlots) & 1u, a.status, 35u)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t raw_row = sRaw + rs * kRawBytes + r * raw_row_bytes<TYPE>();
+                // the chunk's 4 stages; stage J holds blocks 2J (half 0) and 2J+1 (half 1)
+                auto stage = [&](auto J) {
+                    constexpr uint32_t j = decltype(J)::value;
+                    const uint32_t ks = kc * (kRawK / kBK) + j;
+                    if (!ok || ks >= ksteps) return;
+                    const uint32_t s = ks % kS;
+                    if (ks >= kS && !mbar_wait_bounded(&ab_empty[s], ((ks / kS) - 1u) & 1u, a.status, 36u)) {
+                        ok = false;
+                        return;
+                    }
+                    if (half == 0)
+                        dequant_block<TYPE, 2u * j>(raw_row, sA + s * kStageA, r);
+                    else
+                        dequant_block<TYPE, 2u * j + 1u>(raw_row, sA + s * kStageA, r);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[s]);
+                };
+                stage(Idx<0>{});
+                stage(Idx<1>{});
+                stage(Idx<2>{});
+                stage(Idx<3>{});
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[rs]);
+            }
+        }
+        // epilogue: TMEM lanes of this warp's quarter, half of the token columns
+        const uint32_t quarter = warp & 3u;
+        const uint32_t col_half = (warp - 2u) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+        if (mbar_wait_bounded(done, 0, a.status, 37u)) {
+            tc_fence_after();
+            const uint32_t wrow = row0 + quarter * 32u + lane;
+            for (uint32_t cb = 0; cb < kBN / 64u; ++cb) {
+                const uint32_t col = col_half * (kBN / 2u) + cb * 32u;
+                uint32_t v[32];
+                tc_ld_32x32b_x32(tmem_d + ((quarter * 32u) << 16) + col, v);
+                if (wrow < a.rows) {
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; ++i) {
+                        const uint32_t t = tok0 + col + i;
+                        if (t < a.tokens) a.y[static_cast<size_t>(t) * a.ldy + wrow] = __uint_as_float(v[i]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kBN));
+    }
+}
+
+// ---- host side ----------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+template <uint32_t TYPE>
+cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
+                     uint32_t ldy, DeviceStatus* status, cudaStream_t stream) {
+    EncodeTiled enc = encode_fn();
+    if (enc == nullptr) return cudaErrorNotSupported;
+    CUtensorMap mw, mx;
+    const uint64_t rb = row_bytes_of(TYPE, cols);
+    if (TYPE == kF16) {
+        const cuuint64_t dims[2] = {cols, rows}, strides[1] = {rb};
+        const cuuint32_t box[2] = {kBK, kBM}, es[2] = {1, 1};
+        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(w), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    } else {
+        // raw rows as uint16 elements: a 256-element chunk is raw_row_bytes/2 of them
+        const cuuint64_t dims[2] = {rb / 2u, rows}, strides[1] = {rb};
+        const cuuint32_t box[2] = {raw_row_bytes<TYPE>() / 2u, kBM}, es[2] = {1, 1};
+        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        const cuuint64_t dims[2] = {cols, tokens}, strides[1] = {static_cast<cuuint64_t>(cols) * 2u};
+        const cuuint32_t box[2] = {kBK, kBN}, es[2] = {1, 1};
+        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(xh), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    constexpr uint32_t raw_bytes = TYPE == kF16 ? 0u : kBM * raw_row_bytes<TYPE>();
+    constexpr uint32_t kS = stages<TYPE>();
+    const uint32_t smem = 1024u + kS * (kStageA + kStageB) + kRawSlots * raw_bytes + 8u * (3u * kS + 2u * kRawSlots + 1u) + 16u;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    GemmArgs a{};
+    a.y = y;
+    a.rows = rows;
+    a.cols = cols;
+    a.tokens = tokens;
+    a.ldy = ldy;
+    a.status = status;
+    const dim3 grid((rows + kBM - 1) / kBM, (tokens + kBN - 1) / kBN);
+    gemm_tc_kernel<TYPE><<<grid, kThreads, smem, stream>>>(mw, mx, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens) {
+    if (type != kF16 && type != kQ8_0 && type != kQ4_0) return false;
+    if (rows == 0 || tokens == 0 || rows > 0x7FFFFFFFull || tokens > 0x7FFFFFFFull || cols > 0x7FFFFFFFull) return false;
+    if (cols % 32u) return false;
+    const uint64_t rb = row_bytes_of(type, cols);
+    return rb % 16u == 0 && cols % 8u == 0;
+}
+
+cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream) {
+    uint64_t blocks = (n / 4u + 255u) / 256u;
+    if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
+    if (blocks == 0) blocks = 1;
+    x_to_f16_kernel<<<static_cast<uint32_t>(blocks), 256, 0, stream>>>(x, xh, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
+                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream) {
+    if (!gemm_tc_supported(type, rows, cols, tokens)) return cudaErrorInvalidValue;
+    const uint32_t r = static_cast<uint32_t>(rows), c = static_cast<uint32_t>(cols), t = static_cast<uint32_t>(tokens);
+    switch (type) {
+        case kQ8_0: return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        case kQ4_0: return launch_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        case kF16: return launch_t<kF16>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace nedo_gpu

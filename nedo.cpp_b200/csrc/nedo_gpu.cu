@@ -61,6 +61,8 @@ struct DeviceState {
     float* y_pin = nullptr;
     uint64_t xp_cap = 0, yp_cap = 0;
     DeviceStatus* status_pin = nullptr;
+    __half* xh = nullptr;  // fp16 copy of the token vectors for the tensor-core GEMM
+    uint64_t xh_cap = 0;
     std::unordered_map<const void*, Resident> cache;
     std::mutex mu;
 };
@@ -191,6 +193,9 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Batches of at least this many token vectors run as one tensor-core GEMM.
+constexpr uint32_t kTensorCoreMinBatch = 16;
+
 // The one dispatch point for every matvec launch.
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
                     float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream) {
@@ -210,6 +215,17 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
             return 0;
         }
+    }
+    if (batch >= kTensorCoreMinBatch && amax == nullptr && aligned16(w) && aligned16(x) &&
+        gemm_tc_supported(type, rows, cols, batch)) {
+        // tokens as the N dimension of a tcgen05 GEMM (x rounded to fp16 once)
+        const uint64_t n = static_cast<uint64_t>(batch) * cols;
+        if (int rc = ensure_dev(&s->xh, &s->xh_cap, n)) return rc;
+        cudaError_t e = launch_x_to_f16(x, s->xh, n, s->num_sms, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "x to fp16 launch");
+        e = launch_gemm_tc(type, w, s->xh, y, rows, cols, batch, rows, s->status, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
+        return 0;
     }
     if (batch > 1 && aligned16(w) && aligned16(x) && (cols * sizeof(float)) % 16 == 0) {
         StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
@@ -503,7 +519,14 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             return 0;
         }
     }
-    out[0] = 2;
+    if (batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch)) {
+        out[0] = 5;  // tcgen05 GEMM: 128-row x 128-token tiles
+        out[1] = static_cast<uint32_t>(((rows + 127) / 128) * ((batch + 127) / 128));
+        out[2] = 320;
+        out[4] = 128;
+        return 0;
+    }
+    out[0] = batch > 1 ? 3 : 2;
     return 0;
 }
 

@@ -126,6 +126,23 @@ def test_batched_matches_serial_reference(lib, cuda, oracle, t):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"batch item {b}")
 
 
+# Batches of >= 16 vectors run as one tcgen05 GEMM (fp16 x and d*q, fp32
+# accumulation): the same per-element tolerance against the reference's serial
+# matvecs.  Shapes cover ragged token tiles (tiles of 256), ragged row tiles
+# (128) and an odd number of 256-element weight chunks.
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
+@pytest.mark.parametrize("rows,cols,batch", [(300, 2048, 16), (1000, 4096, 64), (129, 1280, 300)])
+def test_batched_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
+    plan = lib.plan_info(t, rows, cols, batch)
+    assert plan["path"] == 5, plan
+    w = B.gen_weight(t, rows, cols, 31 + batch)
+    x = B.gen_x(cols, 31 + batch, batch=batch)
+    y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    ref = oracle.matvec_batch(t, rows, cols, w, x)
+    for b in range(batch):
+        assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
+
+
 def test_lm_head_argmax(lib, cuda, oracle):
     # F16 LM head with the greedy pick fused into the matvec kernel.
     rows, cols = 32000, 2048
