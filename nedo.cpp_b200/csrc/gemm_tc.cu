@@ -139,11 +139,6 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
     return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -497,6 +492,10 @@ bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tok
     if (cols % 32u) return false;
     const uint64_t rb = row_bytes_of(type, cols);
     return rb % 16u == 0 && cols % 8u == 0;
+}
+
+uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens) {
+    return static_cast<uint32_t>(((rows + kBM - 1) / kBM) * ((tokens + kBN - 1) / kBN));
 }
 
 cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream) {

@@ -100,6 +100,7 @@ cudaError_t launch_argmax(const float* v, uint64_t n, ArgmaxScratch* scratch, in
 // shared memory), xh the token vectors in fp16 (launch_x_to_f16), y fp32 with
 // row pitch ldy.  Supported: F16 / Q8_0 / Q4_0, cols % 32 == 0, 16-byte rows.
 bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens);
+uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens);  // CTAs of one launch (128 rows x 256 tokens each)
 cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream);
 cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
                            uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream);

@@ -520,8 +520,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
         }
     }
     if (batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch)) {
-        out[0] = 5;  // tcgen05 GEMM: 128-row x 128-token tiles
-        out[1] = static_cast<uint32_t>(((rows + 127) / 128) * ((batch + 127) / 128));
+        out[0] = 5;  // tcgen05 GEMM: 128-row x 256-token tiles
+        out[1] = gemm_tc_ctas(rows, batch);
         out[2] = 320;
         out[4] = 128;
         return 0;
