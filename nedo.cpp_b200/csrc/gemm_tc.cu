@@ -7,18 +7,22 @@
 // (src/kernels.cpp:162-169).  Here the tokens become the N dimension of one
 // tcgen05 contraction per 128-row weight tile:
 //
+//   * A CTA owns 256 weight rows x 256 tokens: two M=128 MMAs per K step share
+//     the token tile, with both fp32 accumulators in TMEM (2 x 256 columns).
+//     Fewer, larger tiles halve the operand bytes each SM pulls through L2 per
+//     FLOP compared with 128-row tiles.
 //   * W stays in GGUF block layout in HBM.  A TMA tensor map over the row bytes
-//     (uint16 elements, so every 256-element chunk of a Q8_0 / Q4_0 row starts on
-//     a 16-byte boundary) brings 128 rows x 256 elements of raw blocks into
-//     shared memory; eight dequant warps turn each block into fp16 d*q (the
-//     product is exact in fp32 and rounded once to fp16) and write the MMA's A
-//     tiles in the 128-byte-swizzled K-major layout.  F16 weights load straight
+//     (uint16 elements) brings 256 rows x 128 elements of raw blocks into shared
+//     memory; the box starts at the 16-byte boundary at or below the chunk (8
+//     bytes early for odd chunks).  Eight dequant warps, one thread per row, turn
+//     each block into fp16 d*q (exact in fp32, rounded once) and write the A
+//     tiles in the 64-byte-swizzled K-major layout.  F16 weights load straight
 //     into that layout with a swizzled tensor map.
 //   * X is converted once to fp16 (round to nearest) and loaded per stage with a
-//     swizzled tensor map as the B operand (tokens x 64 K).
-//   * One thread issues tcgen05.mma kind::f16 (M=128 weight rows, N=256 tokens,
-//     K=16, fp32 accumulators in TMEM); tcgen05.commit releases the stage.
-//   * The dequant warps then read TMEM (tcgen05.ld 32x32b) and store Y.
+//     swizzled tensor map as the B operand (256 tokens x 32 K).
+//   * One thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16);
+//     tcgen05.commit releases each stage.  The dequant warps then read TMEM
+//     (tcgen05.ld 32x32b) and store Y.
 //
 // fp16 rounding of x and of d*q is the only difference from the reference's
 // fp32 arithmetic (relative 2^-11 per factor); the products are summed in fp32.
@@ -34,20 +38,22 @@
 namespace nedo_gpu {
 namespace {
 
-constexpr uint32_t kBM = 128;         // weight rows per tile (MMA M, TMEM lanes)
-constexpr uint32_t kBN = 256;         // tokens per tile (MMA N, TMEM columns)
-constexpr uint32_t kBK = 64;          // K per stage: one 128-byte fp16 row of a swizzle atom
-constexpr uint32_t kRawK = 256;       // K per raw weight chunk: 8 GGUF blocks
-// A/B stages: 48 KB each; quantised weights also need two raw chunk slots
+constexpr uint32_t kBM = 128;           // weight rows per MMA (M, TMEM lanes)
+constexpr uint32_t kHalves = 2;         // MMAs per K step: a CTA covers 256 weight rows
+constexpr uint32_t kRows = kBM * kHalves;
+constexpr uint32_t kBN = 256;           // tokens per tile (MMA N; TMEM columns per accumulator)
+constexpr uint32_t kBK = 32;            // K per stage: one 64-byte fp16 row of a swizzle atom
+constexpr uint32_t kRawK = 128;         // K per raw weight chunk: 4 GGUF blocks
+// A/B stages: 32 KB each; quantised weights also need two raw chunk slots
 template <uint32_t TYPE>
 constexpr uint32_t stages() {
-    return TYPE == kF16 ? 4u : 3u;
+    return TYPE == kF16 ? 6u : 4u;
 }
 constexpr uint32_t kRawSlots = 2;
 constexpr uint32_t kDeqWarps = 8;     // warps 2..9: dequant, then epilogue
 constexpr uint32_t kThreads = (2 + kDeqWarps) * 32;
-constexpr uint32_t kStageA = kBM * 128;  // 16 KB
-constexpr uint32_t kStageB = kBN * 128;  // 32 KB
+constexpr uint32_t kStageA = kRows * 64;  // 16 KB: two 8 KB halves of 128 rows
+constexpr uint32_t kStageB = kBN * 64;    // 16 KB
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
@@ -65,9 +71,12 @@ template <>
 struct RawBlock<kF16> {  // F16 rows load straight into the A tiles (no raw chunk)
     static constexpr uint32_t kBytes = 64;
 };
+// Bytes of one row of a raw chunk in shared memory: the chunk's kRawK / 32
+// blocks plus 8 bytes, because the box starts at the 16-byte boundary at or
+// below the chunk (4 * 34 and 4 * 18 are 8 mod 16: odd chunks start 8 bytes in).
 template <uint32_t TYPE>
-constexpr uint32_t raw_row_bytes() {  // bytes of one row of a raw chunk (kRawK elements)
-    return kRawK / 32u * RawBlock<TYPE>::kBytes;
+constexpr uint32_t raw_row_bytes() {
+    return kRawK / 32u * RawBlock<TYPE>::kBytes + 8u;
 }
 
 struct GemmArgs {
@@ -119,24 +128,25 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[3
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
-// 1024 bytes (SBO), version 1 (sm_100).  The tile base is 1024-byte aligned.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// Shared-memory matrix descriptor: K-major, 64-byte swizzle, 8-row atoms of
+// 512 bytes (SBO), version 1 (sm_100).  Tile bases are 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
     uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(1u) << 16;            // LBO (unused by swizzled K-major)
-    d |= static_cast<uint64_t>(1024u >> 4) << 32;    // SBO: 8 rows x 128 bytes
-    d |= static_cast<uint64_t>(1u) << 46;            // descriptor version for sm_100
-    d |= static_cast<uint64_t>(2u) << 61;            // SWIZZLE_128B
+    d |= static_cast<uint64_t>(1u) << 16;           // LBO (unused by swizzled K-major)
+    d |= static_cast<uint64_t>(512u >> 4) << 32;    // SBO: 8 rows x 64 bytes
+    d |= static_cast<uint64_t>(1u) << 46;           // descriptor version for sm_100
+    d |= static_cast<uint64_t>(4u) << 61;           // SWIZZLE_64B
     return d;
 }
 
 // kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M x N.
 constexpr uint32_t kIdesc = (1u << 4) | ((kBN >> 3) << 17) | ((kBM >> 4) << 24);
 
-// fp16 tile element (row r, 16-byte chunk c of its 128-byte row) in the
-// 128-byte-swizzled K-major layout: chunk c lands at c ^ (r % 8).
-__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t c) {
-    return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+// fp16 tile element (row r, 16-byte chunk c of its 64-byte row) in the
+// 64-byte-swizzled K-major layout: byte-address bits 4-5 are XORed with bits
+// 7-8, so chunk c of row r lands at c ^ ((r / 2) % 4).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t r, uint32_t c) {
+    return (r >> 3) * 512u + (r & 7u) * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -149,13 +159,14 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     return v;
 }
 
-// Dequantise block BLK (0..7) of row r of a raw chunk into the A stage:
-// elements 32*(BLK%2) .. +32 of the stage's 64-wide K window.  All offsets
-// are compile-time; the block's bytes come from 16-byte aligned loads.
-template <uint32_t TYPE, uint32_t BLK>
-__device__ __forceinline__ void dequant_block(uint32_t raw_row, uint32_t a_stage, uint32_t r) {
+// Dequantise block BLK (0..3) of row r of a raw chunk (SKEW: 0 or 8 bytes of
+// the previous chunk before it) into row r of an A half-tile: the 32 elements
+// of one K stage.  All offsets are compile-time; the block's bytes come from
+// 16-byte aligned loads.
+template <uint32_t TYPE, uint32_t SKEW, uint32_t BLK>
+__device__ __forceinline__ void dequant_block(uint32_t raw_row, uint32_t a_half, uint32_t r) {
     constexpr uint32_t BB = RawBlock<TYPE>::kBytes;
-    constexpr uint32_t start = BLK * BB;           // block offset in the raw row
+    constexpr uint32_t start = SKEW + BLK * BB;    // block offset in the raw row
     constexpr uint32_t base = start & ~15u;        // 16-byte aligned window
     constexpr uint32_t off = start - base;         // 0..14, even
     constexpr uint32_t nchunks = (off + BB + 15u) / 16u;  // 2 (Q4_0) or 3 (Q8_0)
@@ -186,7 +197,6 @@ __device__ __forceinline__ void dequant_block(uint32_t raw_row, uint32_t a_stage
     const uint32_t dbits = pair_bytes(0);
     const __half dh = __ushort_as_half(static_cast<unsigned short>((dbits & 0xFFu) | ((dbits >> 8) & 0xFF00u)));
     const __half2 d2 = __halves2half2(dh, dh);
-    constexpr uint32_t c_first = (BLK & 1u) * 4u;  // 16-byte chunk index in the 128-byte stage row
 #pragma unroll
     for (uint32_t c = 0; c < 4; ++c) {  // 8 elements per 16-byte output chunk
         uint32_t h[4];
@@ -210,7 +220,7 @@ __device__ __forceinline__ void dequant_block(uint32_t raw_row, uint32_t a_stage
             const __half2 p = __hmul2(q, d2);
             h[e] = *reinterpret_cast<const uint32_t*>(&p);
         }
-        sts128(a_stage + sw128_offset(r, c_first + c), h[0], h[1], h[2], h[3]);
+        sts128(a_half + sw64_offset(r, c), h[0], h[1], h[2], h[3]);
     }
 }
 
@@ -243,9 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* const sbase = smem_raw + (s0 - smem_addr(smem_raw));
     constexpr bool kRawW = TYPE != kF16;
     constexpr uint32_t kS = stages<TYPE>();
-    constexpr uint32_t kRawBytes = kRawW ? kBM * raw_row_bytes<TYPE>() : 0u;
-    const uint32_t sA = s0;                       // kS x 16 KB
-    const uint32_t sB = sA + kS * kStageA;        // kS x 32 KB
+    constexpr uint32_t kRawBytes = kRawW ? kRows * raw_row_bytes<TYPE>() : 0u;
+    const uint32_t sA = s0;                       // kS x 16 KB (two 128-row halves)
+    const uint32_t sB = sA + kS * kStageA;        // kS x 16 KB
     const uint32_t sRaw = sB + kS * kStageB;          // kRawSlots x raw chunk
     uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + (sRaw - s0) + kRawSlots * kRawBytes);
     uint64_t* b_full = bars;                  // [kS] X (and F16 W) tiles landed
@@ -257,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t row0 = blockIdx.x * kBM;   // weight rows of this tile
+    const uint32_t row0 = blockIdx.x * kRows;  // weight rows of this tile
     const uint32_t tok0 = blockIdx.y * kBN;   // tokens of this tile
     const uint32_t ksteps = (a.cols + kBK - 1) / kBK;
     const uint32_t chunks = (a.cols + kRawK - 1) / kRawK;
@@ -275,9 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(done, 1);
         fence_barrier_init();
     }
-    if (warp == 1) {  // TMEM: kBN fp32 columns x 128 lanes
+    if (warp == 1) {  // TMEM: two accumulators of kBN fp32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(kBN));
+                     "r"(kHalves * kBN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -299,7 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-                    tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>(kc * (raw_row_bytes<TYPE>() / 2u)),
+                    // the chunk's first byte, rounded down to 16 bytes (uint16 elements)
+                    const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
+                    tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
                                 static_cast<int32_t>(row0), &raw_full[rs]);
                     issued_kc = kc + 1u;
                 }
@@ -336,19 +348,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (kRawW) ok = ok && mbar_wait_bounded(&a_full[s], ph, a.status, 34u);
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t ad = sw128_desc(sA + s * kStageA), bd = sw128_desc(sB + s * kStageB);
+                const uint64_t bd = sw64_desc(sB + s * kStageB);
 #pragma unroll
-                for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // K = 16 per MMA: 32 bytes along the row
-                    tc_mma_f16(tmem_d, ad + 2u * kk, bd + 2u * kk, kIdesc, (ks | kk) != 0u);
+                for (uint32_t h = 0; h < kHalves; ++h) {
+                    const uint64_t ad = sw64_desc(sA + s * kStageA + h * (kBM * 64u));
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // K = 16 per MMA: 32 bytes along the row
+                        tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, kIdesc, (ks | kk) != 0u);
+                }
                 tc_commit(&ab_empty[s]);
             }
             tc_commit(done);  // every MMA issued above has completed when this arrives
         }
     } else {
         // ---------------- dequant warps, then epilogue ----------------
-        const uint32_t dt = threadIdx.x - 64u;  // 0..255
-        const uint32_t r = dt & (kBM - 1u);      // tile row
-        const uint32_t half = dt >> 7;           // which block of each stage's pair
+        const uint32_t r = threadIdx.x - 64u;    // tile row 0..255: one row per thread
+        const uint32_t half = r / kBM;           // which MMA half-tile the row belongs to
         if constexpr (kRawW) {
             bool ok = true;
             for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
@@ -358,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 const uint32_t raw_row = sRaw + rs * kRawBytes + r * raw_row_bytes<TYPE>();
-                // the chunk's 4 stages; stage J holds blocks 2J (half 0) and 2J+1 (half 1)
+                // the chunk's 4 stages; stage J holds block J of every row
                 auto stage = [&](auto J) {
                     constexpr uint32_t j = decltype(J)::value;
                     const uint32_t ks = kc * (kRawK / kBK) + j;
@@ -368,10 +383,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         return;
                     }
-                    if (half == 0)
-                        dequant_block<TYPE, 2u * j>(raw_row, sA + s * kStageA, r);
+                    const uint32_t a_half = sA + s * kStageA + half * (kBM * 64u);
+                    if (kc & 1u)  // odd chunks start 8 bytes into the loaded row
+                        dequant_block<TYPE, 8u, j>(raw_row, a_half, r & (kBM - 1u));
                     else
-                        dequant_block<TYPE, 2u * j + 1u>(raw_row, sA + s * kStageA, r);
+                        dequant_block<TYPE, 0u, j>(raw_row, a_half, r & (kBM - 1u));
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&a_full[s]);
@@ -384,16 +400,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
             }
         }
-        // epilogue: TMEM lanes of this warp's quarter, half of the token columns
+        // epilogue: warps 2..5 read accumulator 0 (rows 0..127), warps 6..9
+        // accumulator 1 (rows 128..255), each its TMEM lane quarter, all tokens
         const uint32_t quarter = warp & 3u;
-        const uint32_t col_half = (warp - 2u) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+        const uint32_t acc = (warp - 2u) >> 2;
         if (mbar_wait_bounded(done, 0, a.status, 37u)) {
             tc_fence_after();
-            const uint32_t wrow = row0 + quarter * 32u + lane;
-            for (uint32_t cb = 0; cb < kBN / 64u; ++cb) {
-                const uint32_t col = col_half * (kBN / 2u) + cb * 32u;
+            const uint32_t wrow = row0 + acc * kBM + quarter * 32u + lane;
+            for (uint32_t col = 0; col < kBN; col += 32u) {
                 uint32_t v[32];
-                tc_ld_32x32b_x32(tmem_d + ((quarter * 32u) << 16) + col, v);
+                tc_ld_32x32b_x32(tmem_d + acc * kBN + ((quarter * 32u) << 16) + col, v);
                 if (wrow < a.rows) {
 #pragma unroll
                     for (uint32_t i = 0; i < 32; ++i) {
@@ -408,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kBN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kHalves * kBN));
     }
 }
 
@@ -439,15 +455,15 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     const uint64_t rb = row_bytes_of(TYPE, cols);
     if (TYPE == kF16) {
         const cuuint64_t dims[2] = {cols, rows}, strides[1] = {rb};
-        const cuuint32_t box[2] = {kBK, kBM}, es[2] = {1, 1};
+        const cuuint32_t box[2] = {kBK, kRows}, es[2] = {1, 1};
         if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(w), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     } else {
         // raw rows as uint16 elements: a 256-element chunk is raw_row_bytes/2 of them
         const cuuint64_t dims[2] = {rb / 2u, rows}, strides[1] = {rb};
-        const cuuint32_t box[2] = {raw_row_bytes<TYPE>() / 2u, kBM}, es[2] = {1, 1};
+        const cuuint32_t box[2] = {raw_row_bytes<TYPE>() / 2u, kRows}, es[2] = {1, 1};
         if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -457,11 +473,11 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
         const cuuint64_t dims[2] = {cols, tokens}, strides[1] = {static_cast<cuuint64_t>(cols) * 2u};
         const cuuint32_t box[2] = {kBK, kBN}, es[2] = {1, 1};
         if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(xh), dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    constexpr uint32_t raw_bytes = TYPE == kF16 ? 0u : kBM * raw_row_bytes<TYPE>();
+    constexpr uint32_t raw_bytes = TYPE == kF16 ? 0u : kRows * raw_row_bytes<TYPE>();
     constexpr uint32_t kS = stages<TYPE>();
     const uint32_t smem = 1024u + kS * (kStageA + kStageB) + kRawSlots * raw_bytes + 8u * (3u * kS + 2u * kRawSlots + 1u) + 16u;
     static bool configured[64] = {};
@@ -479,7 +495,7 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     a.tokens = tokens;
     a.ldy = ldy;
     a.status = status;
-    const dim3 grid((rows + kBM - 1) / kBM, (tokens + kBN - 1) / kBN);
+    const dim3 grid((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN);
     gemm_tc_kernel<TYPE><<<grid, kThreads, smem, stream>>>(mw, mx, a);
     return cudaGetLastError();
 }
@@ -495,7 +511,7 @@ bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tok
 }
 
 uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens) {
-    return static_cast<uint32_t>(((rows + kBM - 1) / kBM) * ((tokens + kBN - 1) / kBN));
+    return static_cast<uint32_t>(((rows + kRows - 1) / kRows) * ((tokens + kBN - 1) / kBN));
 }
 
 cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream) {
