@@ -7,17 +7,26 @@ A step is one pass of the hot path over one batch of synthetic input: one
 dequantize-and-dot matvec (batch 1) over a GGUF weight resident in HBM.
 
 Workloads (default q4_0_11008x4096):
-  q4_0_11008x4096      Q4_0 11008x4096 batch-1 matvec.  With N GPUs the weight is
-                       (N*11008)x4096, row-sharded 11008 rows per GPU, and the y
-                       slices are all-gathered over NCCL: weak scaling.
+  q4_0_11008x4096      Q4_0 11008x4096 batch-1 matvec.  With N GPUs every GPU
+                       streams its own 11008x4096 row block (rows are independent:
+                       no exchange on the data path): weak scaling.
   q8_0_4096x4096       Q8_0 4096x4096 batch-1 matvec (weak scaling as above).
-  f16_head_128000x2048 F16 128000x2048 LM-head matvec with the argmax fused.
-  q4_0_32768x32768     Q4_0 32768x32768, row-sharded over N GPUs + NCCL all-gather
-                       of y: strong scaling (fixed total matrix).
+  f16_head_128000x2048 F16 128000x2048 LM-head matvec with the argmax fused
+                       (weak scaling as above).
+  q4_0_32768x32768     Q4_0 32768x32768, row-sharded over N GPUs with the y slices
+                       all-gathered: the matvec kernel stores its rows on every
+                       peer over NVLink (NCCL where that kernel does not take the
+                       shape): strong scaling (fixed total matrix).
   q8_0_prefill_512x4096x14336
                        prompt-shaped batch: 512 token vectors through one Q8_0
                        14336x4096 weight (the tcgen05 GEMM), TFLOP/s; replicas
                        at N > 1.
+  decode_sweep_24x1536_b1, _b8, _b32
+                       every matvec of a synthetic 24-layer decoder (d_model 1536:
+                       q/k/v/o 1536x1536, gate/up 4096x1536, down 1536x4096, Q8_0)
+                       plus an F16 64000x1536 head, for 1, 8 or 32 tokens per step
+                       (the head takes the argmax at batch 1); GB/s with each
+                       weight counted once per step, per-matrix GB/s in the line.
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max over
@@ -55,13 +64,30 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1400.0
 
 WORKLOADS = {
-    "q4_0_11008x4096": dict(type=B.Q4_0, rows=11008, cols=4096, shard="weak", argmax=False),
-    "q8_0_4096x4096": dict(type=B.Q8_0, rows=4096, cols=4096, shard="weak", argmax=False),
-    "f16_head_128000x2048": dict(type=B.F16, rows=128000, cols=2048, shard="weak", argmax=True),
+    "q4_0_11008x4096": dict(type=B.Q4_0, rows=11008, cols=4096, shard="replica", argmax=False),
+    "q8_0_4096x4096": dict(type=B.Q8_0, rows=4096, cols=4096, shard="replica", argmax=False),
+    "f16_head_128000x2048": dict(type=B.F16, rows=128000, cols=2048, shard="replica", argmax=True),
     "q4_0_32768x32768": dict(type=B.Q4_0, rows=32768, cols=32768, shard="strong", argmax=False),
     "q8_0_prefill_512x4096x14336": dict(type=B.Q8_0, rows=14336, cols=4096, shard="replica", argmax=False,
                                         batch=512),
 }
+for _b in (1, 8, 32):
+    WORKLOADS[f"decode_sweep_24x1536_b{_b}"] = dict(kind="sweep", type=B.Q8_0, layers=24, d=1536, ff=4096,
+                                                    head=64000, batch=_b, shard="replica", argmax=_b == 1,
+                                                    rows=1536, cols=1536)
+
+
+def sweep_matrices(wl):
+    """(name, type, rows, cols) of one decode step, in call order."""
+    d, ff = wl["d"], wl["ff"]
+    layer = [("q", d, d), ("k", d, d), ("v", d, d), ("o", d, d), ("gate", ff, d), ("up", ff, d), ("down", d, ff)]
+    mats = [(f"{n}{li}", wl["type"], r, c) for li in range(wl["layers"]) for n, r, c in layer]
+    return mats + [("head", B.F16, wl["head"], d)]
+
+
+def sweep_bytes(wl, batch):
+    """Algorithmic bytes of one step: every weight once, x and y per token."""
+    return sum(r * B.row_bytes(t, c) + batch * 4 * (r + c) for _, t, r, c in sweep_matrices(wl))
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures
 # summarised under profiles/ (None where no capture exists for the workload).
@@ -221,6 +247,16 @@ def cpu_baseline(wl, rows_total, budget_s=10.0):
 def run_reference_arm(args, wl, world, rank):
     if rank != 0:
         return
+    if wl.get("kind") == "sweep":
+        cb = sweep_cpu(wl, budget_s=min(20.0, 0.05 * args.steps + 2.0))
+        line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks)",
+                "config": {"workload": args.workload, "batch": batch_of(wl)},
+                "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                            "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     _, rows_total = shard_rows(wl, world)
     nvec = CPU_BATCH_SAMPLE if batch_of(wl) > 1 else 1
     fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7, nvec=nvec)
@@ -255,8 +291,10 @@ def workload_config(name, wl, world):
                 f"(prefill GEMM, M={batch_of(wl)} K={wl['cols']} N={wl['rows']})")
         if world > 1:
             desc += f", {world} independent replicas"
+    elif world > 1 and wl["shard"] == "replica":
+        desc += f", {world} independent {rows}-row blocks (one per GPU, no exchange)"
     elif world > 1:
-        desc += f", row-sharded {rows} rows per GPU + NCCL all-gather of y"
+        desc += f", row-sharded {rows} rows per GPU + all-gather of y"
     if wl["argmax"]:
         desc += ", argmax fused"
     return {"workload": name, "description": desc, "type": t, "rows_total": rows_total, "rows_per_gpu": rows,
@@ -292,7 +330,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     import torch.distributed as dist
 
     import nedo_gpu
-    from nedo_gpu.shard import ShardedMatvec
+    from nedo_gpu.shard import FusedShardedMatvec, ShardedMatvec
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -324,15 +362,26 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         else:
             lib.matvec_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), nb, s)
 
-    # N > 1: this rank's rows, then the NCCL all-gather of the y slices
-    # (replica workloads run independently on every GPU: no collective)
-    sm = ShardedMatvec(t, rows_total, cols) if world > 1 and wl["shard"] != "replica" else None
+    # N > 1: this rank's rows, then every rank gets all of y -- fused into the
+    # int8 tensor-pipe kernel as NVLink peer stores where it takes the shape,
+    # else an NCCL all-gather (replica workloads run independently: no collective)
+    sm = fm = None
+    collective = None
+    if world > 1 and wl["shard"] != "replica":
+        if plan.get("path") == 4 and nb == 1:
+            fm = FusedShardedMatvec(lib, t, rows_total, cols, device)
+            collective = "fused: rows stored on every peer over NVLink by the matvec kernel + completion wait"
+        else:
+            sm = ShardedMatvec(t, rows_total, cols)
+            collective = "NCCL all-gather of the y slices"
 
     def step(k):
-        if sm is None:
-            launch(k, stream.cuda_stream)
-        else:
+        if fm is not None:
+            fm.run(w[k % copies].data_ptr(), x.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        elif sm is not None:
             sm.run(lambda xv, yl: launch(k, stream.cuda_stream), x, y, y_full)
+        else:
+            launch(k, stream.cuda_stream)
 
     def barrier():
         if world > 1:
@@ -359,13 +408,14 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
             launch(k, torch.cuda.current_stream().cuda_stream)
     graph.replay()
     torch.cuda.synchronize()
-    # N > 1: the whole step (matvec + NCCL all-gather) as one graph of K steps;
-    # every rank captures the same collectives in the same order
+    # N > 1: the whole step (matvec + all-gather) as one graph of K steps (K
+    # rounded to even: the fused path alternates two gathered buffers); every
+    # rank captures the same collectives in the same order
     step_graph = None
     if world > 1:
         step_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(step_graph, stream=stream):
-            for k in range(args.steps):
+            for k in range(args.steps + (args.steps & 1)):
                 step(k)
         step_graph.replay()
         torch.cuda.synchronize()
@@ -391,6 +441,8 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     torch.cuda.synchronize()
     barrier()
     region_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    if world > 1:
+        region_ms *= args.steps / (args.steps + (args.steps & 1))
     clocks = sampler.stop()
 
     # kernel-only timing (all ranks, for the roofline)
@@ -411,7 +463,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     value = units_total / (ms_per_step * 1e-3) / scale
 
     # ---- end to end through the C ABI host entry point
-    e2e = e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream)
+    e2e = e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream, fm)
 
     tensor = nb > 1
     peak, peak_kind = peaks(tensor)
@@ -430,7 +482,7 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
                        l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
                           f"> 4x L2)", graph="K steps (matvec" + (" + NCCL all-gather" if world > 1 else "")
                           + ") captured as one CUDA graph",
-                       pdl=True, plan=plan),
+                       pdl=True, plan=plan, **({"collective": collective} if collective else {})),
         "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
                      "launch_us": round(kernel_ms * 1e3, 3),
@@ -446,7 +498,189 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream):
+def run_sweep_arm(args, wl, world, rank, local_rank):
+    """Decode sweep: every matvec of one decoder step (plus the head) per step,
+    all weights resident (918 MB: more than 4x L2, so each step reads HBM)."""
+    import torch
+    import torch.distributed as dist
+
+    import nedo_gpu
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    lib = nedo_gpu.load()
+    lib.set_pdl(True)
+    nb = batch_of(wl)
+    mats = sweep_matrices(wl)
+    ws = [make_weights(torch, t, r, c, 1, seed=2000 + 7 * i + rank, device=device)[0]
+          for i, (_, t, r, c) in enumerate(mats)]
+    d, ff = wl["d"], wl["ff"]
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    xd = torch.randn((nb, d), generator=g, device=device)
+    xf = torch.randn((nb, ff), generator=g, device=device)
+    yd = torch.empty((nb, d), device=device)
+    yf = torch.empty((nb, ff), device=device)
+    logits = torch.empty((nb, wl["head"]), device=device)
+    idx = torch.zeros(1, dtype=torch.int64, device=device)
+    val = torch.zeros(1, dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device=device)
+
+    def one(i, s):
+        name, t, r, c = mats[i]
+        x = xf if c == ff else xd
+        y = logits if name == "head" else (yf if r == ff else yd)
+        if name == "head" and wl["argmax"]:
+            lib.matvec_argmax_dev(t, r, c, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(), idx.data_ptr(),
+                                  val.data_ptr(), s)
+        else:
+            lib.matvec_dev(t, r, c, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(), nb, s)
+
+    def step(s):
+        for i in range(len(mats)):
+            one(i, s)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        tt = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    lib.status(stream.cuda_stream)
+    steps = max(1, min(args.steps, 50))  # about 1 ms per step
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(steps):
+            step(torch.cuda.current_stream().cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    while time.perf_counter() < soak_end:
+        graph.replay()
+        torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_per_step = max_over_ranks(ev0.elapsed_time(ev1)) / steps
+    clocks = sampler.stop()
+    del graph
+    lib.status(stream.cuda_stream)
+
+    # per matrix kind: the 24 layers' launches of one kind (or the head) as one graph
+    kinds = {}
+    for i, (name, t, r, c) in enumerate(mats):
+        kinds.setdefault(name.rstrip("0123456789"), []).append(i)
+    per_kind = {}
+    for kind, ids in kinds.items():
+        kg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kg, stream=stream):
+            for _ in range(3):
+                for i in ids:
+                    one(i, torch.cuda.current_stream().cuda_stream)
+        kg.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            kg.replay()
+            b.record(stream)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / (3 * len(ids))
+        _, t, r, c = mats[ids[0]]
+        byts = r * B.row_bytes(t, c) + nb * 4 * (r + c)
+        per_kind[f"{kind} {B.TYPE_NAMES[t]} {r}x{c}"] = {"us": round(us, 3), "GB/s": round(byts / us / 1e3, 1),
+                                                       "path": lib.plan_info(t, r, c, nb)["path"]}
+        del kg
+
+    units_total = sweep_bytes(wl, nb) * world
+    value = units_total / (ms_per_step * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    launches = sum(nb if (lib.plan_info(t, r, c, nb)["path"] in (3, 4) and nb > 1) else
+                   (2 if lib.plan_info(t, r, c, nb)["path"] == 5 else 1) for _, t, r, c in mats)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
+        "config": {"workload": args.workload,
+                   "description": f"{wl['layers']}-layer d_model {d} decoder step: {len(mats) - 1} Q8_0 matvecs + "
+                                  f"F16 {wl['head']}x{d} head, {nb} token(s) per step",
+                   "batch": nb, "weight_bytes_per_step": sum(r * B.row_bytes(t, c) for _, t, r, c in mats),
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "918 MB of weights, all resident: each step streams them from HBM (> 4x L2)",
+                   "graph": f"{steps} steps of {len(mats)} matvecs captured as one CUDA graph", "pdl": True,
+                   "per_matrix": per_kind},
+        "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / world / peak, 4), "traffic": None, "peak_source": peak_kind,
+                     "launch_us": round(ms_per_step * 1e3, 3), "bytes_per_step": sweep_bytes(wl, nb)},
+        "e2e": None,
+        "gpu_launches": steps * launches,
+        "clocks": clocks,
+    }
+    # end to end: pinned host x in, the step, pinned logits out
+    x_pin = torch.randn((nb, d)).pin_memory()
+    l_pin = torch.empty((nb, wl["head"])).pin_memory()
+    reps = 5
+    with torch.cuda.stream(stream):
+        xd.copy_(x_pin, non_blocking=True)
+        step(stream.cuda_stream)
+        l_pin.copy_(logits, non_blocking=True)
+    stream.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        with torch.cuda.stream(stream):
+            xd.copy_(x_pin, non_blocking=True)
+            step(stream.cuda_stream)
+            l_pin.copy_(logits, non_blocking=True)
+        stream.synchronize()
+    sec = max_over_ranks(time.perf_counter() - t0) / reps
+    line["e2e"] = {"value": round(units_total / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * nb * d,
+                   "d2h_bytes_per_step": 4 * nb * wl["head"], "path": "pinned H2D + 169 nedo_gpu_matvec_dev + D2H",
+                   "ms_per_step": round(sec * 1e3, 4)}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = sweep_cpu(wl, budget_s=10.0)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def sweep_cpu(wl, budget_s=10.0):
+    """The reference CPU kernels over one token of the sweep (all 169 matvecs)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    mats = sweep_matrices(wl)
+    data = [(t, r, c, B.gen_weight(t, r, c, 3000 + i), B.gen_x(c, 3000 + i)) for i, (_, t, r, c) in enumerate(mats)]
+    if O.Reference.available():
+        ref, kind, cores = O.Reference(), "reference", host_cores()
+        ref.set_threads(cores)
+    else:
+        ref, kind, cores = O.Oracle(), "port", 1
+
+    def fn():
+        for t, r, c, w, x in data:
+            ref.matvec(t, r, c, w, x)
+
+    sec, n = time_cpu(fn, budget_s, 1000)
+    units = sweep_bytes(wl, 1)
+    return {"value": round(units / sec / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{n} x one token through all {len(mats)} matvecs ({sec * 1e3:.2f} ms each, {n * sec:.1f} s)"}
+
+
+def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream, fm=None):
     t, cols = wl["type"], wl["cols"]
     nb = batch_of(wl)
     if nb > 1:
@@ -483,15 +717,23 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
                 "d2h_bytes_per_step": 4 * nb * rows,
                 "path": "pinned H2D + nedo_gpu_matvec_dev(batch) + D2H", "ms_per_step": round(sec * 1e3, 4)}
     x_host = np.random.default_rng(7).standard_normal(cols, dtype=np.float32)
-    n_host = min(copies, 8) if world == 1 else 1
-    if world == 1:
+    if world == 1 or wl["shard"] == "replica":
+        # the host entry point (x and y in host memory) on every rank's own block
+        n_host = min(copies, 8)
         hosts = [w[i].cpu().numpy() for i in range(n_host)]
         for h in hosts:  # residency: first call uploads
             lib.matvec(t, rows, cols, h, x_host)
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
         for k in range(args.steps):
             y_host = lib.matvec(t, rows, cols, hosts[k % n_host], x_host)
-        sec = (time.perf_counter() - t0) / args.steps
+        sec = time.perf_counter() - t0
+        if world > 1:
+            tt = torch.tensor([sec], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            sec = float(tt.item())
+        sec /= args.steps
         assert y_host.shape == (rows,)
         for h in hosts:
             lib.weight_evict(h)
@@ -513,9 +755,12 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
     def one(k):
         with torch.cuda.stream(stream):
             xd.copy_(x_pin, non_blocking=True)
-            sm.run(lambda xv, yl: lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xv.data_ptr(),
-                                                 yl.data_ptr(), 1, stream.cuda_stream), xd, y, y_full)
-            y_pin.copy_(y_full, non_blocking=True)
+            if fm is not None:
+                yf = fm.run(w[k % copies].data_ptr(), xd.data_ptr(), stream.cuda_stream)
+            else:
+                yf = sm.run(lambda xv, yl: lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xv.data_ptr(),
+                                                          yl.data_ptr(), 1, stream.cuda_stream), xd, y, y_full)
+            y_pin.copy_(yf, non_blocking=True)
         stream.synchronize()
 
     for k in range(3):
@@ -530,7 +775,9 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
     sec = float(tt.item()) / args.steps
     bytes_total = algorithmic_bytes(t, rows_total, cols)
     return {"value": round(bytes_total / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * cols,
-            "d2h_bytes_per_step": 4 * rows_total, "path": "pinned H2D + nedo_gpu_matvec_dev + NCCL all-gather + D2H",
+            "d2h_bytes_per_step": 4 * rows_total,
+            "path": "pinned H2D + " + ("nedo_gpu_matvec_allgather_dev + wait" if fm is not None else
+                                       "nedo_gpu_matvec_dev + NCCL all-gather") + " + D2H",
             "ms_per_step": round(sec * 1e3, 4)}
 
 
@@ -566,7 +813,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_gpu_arm(args, wl, world, rank, local_rank)
+        if wl.get("kind") == "sweep":
+            run_sweep_arm(args, wl, world, rank, local_rank)
+        else:
+            run_gpu_arm(args, wl, world, rank, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

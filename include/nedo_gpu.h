@@ -147,6 +147,27 @@ NEDO_GPU_API int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* in
 NEDO_GPU_API int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev,
                                 void* stream);
 
+/* Row-sharded matvec with the all-gather of y fused into it (one process
+ * per GPU; rows are independent, src/kernels.cpp:166-168).  Computes this
+ * rank's rows into y_dev like nedo_gpu_matvec_dev and also stores each row at
+ * peer_y[k] + row_offset + r on every peer k (peer device addresses, e.g. from
+ * CUDA IPC or symmetric memory, reachable over NVLink), then adds 1 per CTA to
+ * each peer's 32-bit word peer_signal[k].  Q8_0 / Q4_0 shapes of the int8
+ * tensor-pipe kernel only (plan_info path 4); at most 7 peers.  A receiver
+ * calls nedo_gpu_allgather_wait_dev before reading the gathered y.  No
+ * reference counterpart: the reference runs on one CPU. */
+NEDO_GPU_API int nedo_gpu_matvec_allgather_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev,
+                                  const float* x_dev, float* y_dev, const uint64_t* peer_y,
+                                  const uint64_t* peer_signal, uint32_t npeers, uint64_t row_offset, void* stream);
+
+/* Wait on `stream` (one GPU thread, bounded to 2 s; a timeout sets the status
+ * word read by nedo_gpu_status) until *signal_dev has advanced by `increment`
+ * (peers x CTAs of their launches) past *expected_dev, then advance
+ * *expected_dev.  Both words start at zero; the caller keeps them per
+ * receiving buffer. */
+NEDO_GPU_API int nedo_gpu_allgather_wait_dev(uint32_t* signal_dev, uint32_t* expected_dev, uint32_t increment,
+                                void* stream);
+
 /* embedding_row for rows [row_begin, row_begin + row_count) into
  * out_dev[row_count][cols]; bit-identical to the reference. */
 NEDO_GPU_API int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, uint64_t row_begin,

@@ -1,0 +1,65 @@
+// allgather.cu -- completion wait of the fused all-gather.
+//
+// A row-sharded matvec (rows are independent: reference src/kernels.cpp:166-168)
+// running with a PeerGather stores its rows straight into every peer's gathered
+// y over NVLink and, per CTA, adds 1 to each peer's signal word after a
+// system-scope fence.  This one-thread kernel runs next on the receiving
+// rank's stream: it waits until its signal word has advanced by `increment`
+// (peers x CTAs per launch) past the expected value kept in device memory,
+// then advances that value, so the same launch works unchanged in a CUDA graph
+// replayed many times.  The wait is bounded (2 s); on timeout it records the
+// failure in DeviceStatus and returns.
+//
+// With programmatic dependent launch the wait kernel starts while this rank's
+// matvec is still running (its CTA fits beside the matvec's), so the peers'
+// signals are watched as they arrive; griddepcontrol.wait then covers this
+// rank's own rows before the kernel ends, and the next kernel on the stream
+// may begin its prologue as soon as the wait kernel starts.
+#include "common.cuh"
+#include "launch.h"
+
+namespace nedo_gpu {
+namespace {
+
+__global__ void gather_wait_kernel(uint32_t* signal, uint32_t* expected, uint32_t increment, DeviceStatus* status) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (threadIdx.x != 0) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+    const uint32_t target = *expected + increment;  // wraps with the counter
+    volatile uint32_t* sig = signal;
+    const uint64_t t0 = global_timer_ns();
+    // counters wrap: "reached" is a non-negative signed distance
+    while (static_cast<int32_t>(*sig - target) < 0) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (atomicOr(&status->flags, kErrWaitTimeout) == 0u) status->where = 40u;
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            return;
+        }
+        __nanosleep(200);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // this rank's own rows are complete
+    // acquire: the peers' stores that preceded their signal are visible to
+    // every later kernel on this stream
+    __threadfence_system();
+    *expected = target;
+}
+
+}  // namespace
+
+cudaError_t launch_gather_wait(uint32_t* signal, uint32_t* expected, uint32_t increment, DeviceStatus* status,
+                               cudaStream_t stream, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gather_wait_kernel, signal, expected, increment, status);
+}
+
+}  // namespace nedo_gpu

@@ -62,6 +62,14 @@ struct ImmaArgs {
     uint32_t slots;
     uint32_t slot_bytes;
     DeviceStatus* status;
+    // Fused all-gather (npeers > 0): each finished y row is also stored at
+    // peer_y[k][peer_row_offset + row] on every peer (NVLink peer stores), and
+    // every CTA adds 1 to each peer's counter peer_signal[k] once its rows are
+    // visible system-wide.
+    uint32_t npeers;
+    uint64_t peer_row_offset;
+    float* peer_y[kMaxPeers];
+    uint32_t* peer_signal[kMaxPeers];
 };
 
 constexpr uint32_t kTileRows = 16;  // rows per tile: the M of one IMMA
@@ -428,10 +436,8 @@ __global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gem
                             const float* rr = red + static_cast<size_t>(slot) * W * 16u + lane;
                             float v = 0.f;
                             for (uint32_t k = 0; k < W; ++k) v += rr[k * 16u];
-                            if (!MULTI || c == 0)
-                                a.y[row0 + lane] = v;
-                            else
-                                a.y[row0 + lane] += v;
+                            if (MULTI && c > 0) v += a.y[row0 + lane];
+                            a.y[row0 + lane] = v;
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&empty[slot]);
@@ -443,6 +449,21 @@ __global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gem
                 parity ^= 1u;
             }
         }
+    }
+    if (a.npeers != 0u && warp == 0 && ok) {
+        // This CTA's rows, all written by warp 0, go to every peer as coalesced
+        // stores off the tile pipeline; then lane 0 publishes the CTA on each
+        // peer with a system-scope release add (ordered after the whole warp's
+        // stores by the warp barrier).
+        __syncwarp();
+        for (uint64_t r = row_begin + lane; r < row_end; r += 32u) {
+            const float v = __ldcg(a.y + r);
+            for (uint32_t k = 0; k < a.npeers; ++k) a.peer_y[k][a.peer_row_offset + r] = v;
+        }
+        __syncwarp();
+        if (lane == 0)
+            for (uint32_t k = 0; k < a.npeers; ++k)
+                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_signal[k]) : "memory");
     }
 }
 
@@ -588,8 +609,17 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
 }
 
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
-                        DeviceStatus* status, cudaStream_t stream, bool pdl) {
+                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather) {
     ImmaArgs a{};
+    if (gather != nullptr) {
+        if (gather->npeers > kMaxPeers) return cudaErrorInvalidValue;
+        a.npeers = gather->npeers;
+        a.peer_row_offset = gather->row_offset;
+        for (uint32_t k = 0; k < gather->npeers; ++k) {
+            a.peer_y[k] = gather->peer_y[k];
+            a.peer_signal[k] = gather->peer_signal[k];
+        }
+    }
     a.w = static_cast<const uint8_t*>(w);
     a.x = x;
     a.y = y;

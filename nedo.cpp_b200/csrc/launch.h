@@ -80,8 +80,24 @@ struct ImmaTuning {
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
                    const ImmaTuning* tune = nullptr);
+
+// Fused all-gather of a row-sharded matvec over NVLink: the kernel also stores
+// its rows into every peer's gathered y and counts each finished CTA on the
+// peer's signal word (see launch_gather_wait).
+constexpr uint32_t kMaxPeers = 7;
+struct PeerGather {
+    uint32_t npeers = 0;
+    uint64_t row_offset = 0;          // this rank's first row in the gathered y
+    float* peer_y[kMaxPeers] = {};     // each peer's gathered y (peer device pointers)
+    uint32_t* peer_signal[kMaxPeers] = {};
+};
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
-                        DeviceStatus* status, cudaStream_t stream, bool pdl);
+                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr);
+
+// One thread waits (bounded, 2 s) until *signal has advanced by `increment`
+// past *expected, then advances *expected: the peers' rows are visible after it.
+cudaError_t launch_gather_wait(uint32_t* signal, uint32_t* expected, uint32_t increment, DeviceStatus* status,
+                               cudaStream_t stream, bool pdl);
 
 // Any shape the streaming kernel does not take (odd row sizes, unaligned
 // pointers): one warp per row, byte-granular loads.  x is [batch][ldx], y [batch][ldy].

@@ -227,6 +227,19 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
         if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
         return 0;
     }
+    if (batch > 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
+        // small batches of quantised rows: the int8 tensor-pipe matvec per vector
+        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+        if (ip.ok) {
+            for (uint32_t b = 0; b < batch; ++b) {
+                cudaError_t e = launch_imma(ip, w, x + static_cast<uint64_t>(b) * cols,
+                                            y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, stream,
+                                            g_pdl.load() != 0);
+                if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch");
+            }
+            return 0;
+        }
+    }
     if (batch > 1 && aligned16(w) && aligned16(x) && (cols * sizeof(float)) % 16 == 0) {
         StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
         if (plan.ok) {
@@ -463,6 +476,46 @@ int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_d
     return 0;
 }
 
+int nedo_gpu_matvec_allgather_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
+                                  float* y_dev, const uint64_t* peer_y, const uint64_t* peer_signal, uint32_t npeers,
+                                  uint64_t row_offset, void* stream) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0) return 0;
+    if (!w_dev || !x_dev || !y_dev || (npeers && (!peer_y || !peer_signal)))
+        return fail(NEDO_GPU_ERR_ARG, "matvec_allgather_dev: null pointer");
+    if (npeers > kMaxPeers) return fail(NEDO_GPU_ERR_ARG, "matvec_allgather_dev: more than 7 peers");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    ImmaPlan ip;
+    if ((type == kQ8_0 || type == kQ4_0) && aligned16(w_dev) && aligned16(x_dev))
+        ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+    if (!ip.ok)
+        return fail(NEDO_GPU_ERR_ARG,
+                    "matvec_allgather_dev: the fused all-gather needs a Q8_0/Q4_0 shape of the int8 tensor-pipe kernel");
+    PeerGather g;
+    g.npeers = npeers;
+    g.row_offset = row_offset;
+    for (uint32_t k = 0; k < npeers; ++k) {
+        g.peer_y[k] = reinterpret_cast<float*>(static_cast<uintptr_t>(peer_y[k]));
+        g.peer_signal[k] = reinterpret_cast<uint32_t*>(static_cast<uintptr_t>(peer_signal[k]));
+    }
+    cudaError_t e = launch_imma(ip, w_dev, x_dev, y_dev, rows, cols, s->status, static_cast<cudaStream_t>(stream),
+                                g_pdl.load() != 0, &g);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch (all-gather)");
+    return 0;
+}
+
+int nedo_gpu_allgather_wait_dev(uint32_t* signal_dev, uint32_t* expected_dev, uint32_t increment, void* stream) {
+    if (!signal_dev || !expected_dev) return fail(NEDO_GPU_ERR_ARG, "allgather_wait_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    cudaError_t e = launch_gather_wait(signal_dev, expected_dev, increment, s->status, static_cast<cudaStream_t>(stream),
+                                       g_pdl.load() != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "all-gather wait launch");
+    return 0;
+}
+
 int nedo_gpu_dequant_rows_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, uint64_t row_begin,
                               uint64_t row_count, float* out_dev, void* stream) {
     if (row_begin >= rows || row_count > rows - row_begin) return fail(NEDO_GPU_ERR_ROW, "bad embedding row");
@@ -491,7 +544,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
-    if (batch <= 1 && (type == kQ8_0 || type == kQ4_0)) {
+    const bool tc = batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch);
+    if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // one int8 tensor-pipe launch per vector
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
         if (ip.ok) {
             out[0] = 4;
@@ -519,7 +573,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             return 0;
         }
     }
-    if (batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch)) {
+    if (tc) {
         out[0] = 5;  // tcgen05 GEMM: 128-row x 256-token tiles
         out[1] = gemm_tc_ctas(rows, batch);
         out[2] = 320;

@@ -44,6 +44,8 @@ EXPORTS = (
     "nedo_gpu_matvec_argmax_dev",
     "nedo_gpu_argmax_dev",
     "nedo_gpu_argmax_dev_noalloc",
+    "nedo_gpu_matvec_allgather_dev",
+    "nedo_gpu_allgather_wait_dev",
     "nedo_gpu_dequant_rows_dev",
     "nedo_gpu_status",
     "nedo_gpu_plan_info",
@@ -60,6 +62,7 @@ class NedoGpuError(RuntimeError):
 
 _u32, _u64, _i32, _vp = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p
 _f32p = ctypes.POINTER(ctypes.c_float)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
 
 _SIGNATURES = {
     "nedo_gpu_version": ([], _i32),
@@ -74,6 +77,8 @@ _SIGNATURES = {
     "nedo_gpu_matvec_argmax_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev": ([_vp, _u64, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev_noalloc": ([_vp, _u64, _vp, _vp, _vp], _i32),
+    "nedo_gpu_matvec_allgather_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _u64p, _u64p, _u32, _u64, _vp], _i32),
+    "nedo_gpu_allgather_wait_dev": ([_vp, _vp, _u32, _vp], _i32),
     "nedo_gpu_dequant_rows_dev": ([_u32, _u64, _u64, _vp, _u64, _u64, _vp, _vp], _i32),
     "nedo_gpu_status": ([_vp], _i32),
     "nedo_gpu_plan_info": ([_u32, _u64, _u64, _u32, ctypes.POINTER(_u32), _i32], _i32),
@@ -153,6 +158,19 @@ class Library:
         """argmax_dev with no allocation (a fixed device array of the library;
         overlapping calls on one device race; first call outside stream capture)."""
         self._check(self.lib.nedo_gpu_argmax_dev_noalloc(v_ptr, n, index_ptr, value_ptr, stream))
+
+    def matvec_allgather_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, peer_y, peer_signal, row_offset,
+                             stream=0) -> None:
+        """This rank's rows into y_ptr, also stored on every peer (peer_y[k] + row_offset) with a
+        per-CTA count on each peer's signal word."""
+        n = len(peer_y)
+        py = (ctypes.c_uint64 * max(n, 1))(*peer_y)
+        ps = (ctypes.c_uint64 * max(n, 1))(*peer_signal)
+        self._check(self.lib.nedo_gpu_matvec_allgather_dev(type_, rows, cols, w_ptr, x_ptr, y_ptr, py, ps, n,
+                                                           row_offset, stream))
+
+    def allgather_wait_dev(self, signal_ptr, expected_ptr, increment, stream=0) -> None:
+        self._check(self.lib.nedo_gpu_allgather_wait_dev(signal_ptr, expected_ptr, increment, stream))
 
     def dequant_rows_dev(self, type_, rows, cols, w_ptr, row_begin, row_count, out_ptr, stream=0) -> None:
         self._check(self.lib.nedo_gpu_dequant_rows_dev(type_, rows, cols, w_ptr, row_begin, row_count, out_ptr,
