@@ -429,27 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---- host side ----------------------------------------------------------
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-    static EncodeTiled fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
-    });
-    return fn;
-}
-
 template <uint32_t TYPE>
 cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
                      uint32_t ldy, DeviceStatus* status, cudaStream_t stream) {
-    EncodeTiled enc = encode_fn();
+    EncodeTiled enc = encode_tiled_fn();
     if (enc == nullptr) return cudaErrorNotSupported;
     CUtensorMap mw, mx;
     const uint64_t rb = row_bytes_of(TYPE, cols);
@@ -501,6 +484,19 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
 }
 
 }  // namespace
+
+EncodeTiled encode_tiled_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
 
 bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens) {
     if (type != kF16 && type != kQ8_0 && type != kQ4_0) return false;

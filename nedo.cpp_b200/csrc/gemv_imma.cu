@@ -23,14 +23,30 @@
 //                             high = 16..31), one IMMA per nibble half.
 //   B (32 x 8, col-major)   = x limbs, block-diagonal: column n = 4*block + limb.
 //   D (16 x 8, s32)         = per row, per block, per limb integer dots.
-// A warp owns a fixed slice of the columns (its x limbs stay in registers while
-// the CTA streams its rows) and all warps of a CTA share each 16-row tile,
-// which a producer warp streams from HBM into a shared-memory ring with
-// cp.async.bulk (one copy per row, 16 lanes issuing; no multicast).  Rows
-// longer than 15 warps x 8 pairs are cut into column chunks processed one
-// after the other (x limbs rebuilt per chunk, y accumulated in chunk order).
-// Every wait is bounded; a CTA-wide abort flag stops every warp after the
-// first timed-out wait.
+// The x side of every IMMA (the B registers of each lane, the per-column
+// scale 2^(7*(2-l)-e) and, for Q4_0, the "-8 * sum L" start value of the
+// accumulators) is precomputed once per launch into a shared-memory table in
+// fragment order, so a lane fetches its B operand of a block pair with one
+// 8-byte load.
+//
+// Streaming.  A CTA owns a contiguous run of 16-row tiles.  A unit of work is
+// one segment of seg_pairs block pairs of one tile: a single 2D tensor-map
+// copy (cp.async.bulk.tensor, no multicast) of 16 rows x seg_pairs pairs into
+// one slot of a shared-memory ring, with the box row padded to an odd multiple
+// of 16 bytes so the eight fragment rows of an operand load sit in distinct
+// banks.  Boxes overhanging the row end or the last row read zeros (no memory
+// traffic).  Consumer warps are independent: warp w owns tiles w, w+W, ... of
+// the CTA and runs every segment of such a tile, accumulating its rows in
+// registers, then stores them.  Rows longer than the table holds are cut into
+// column groups processed one after the other (the table is rebuilt between
+// groups and y accumulates in group order; the same warp owns a tile in every
+// group).
+//
+// Two CTA shapes: 8 consumer warps within 113 KB of shared memory, so two CTAs
+// fit on an SM (with programmatic dependent launch the next matvec's CTA
+// streams its first units while this one computes), or a CTA that has the SM
+// alone with a deeper ring.  Every wait is bounded; a CTA-wide abort flag stops
+// every warp after the first timed-out wait.
 #include <math.h>
 
 #include "common.cuh"
@@ -39,28 +55,29 @@
 namespace nedo_gpu {
 namespace {
 
-// Consumer warps per CTA (+1 producer warp).  8 block pairs per warp keep 48
-// x registers live and need the 128-register budget of 512 threads (15
-// consumers); 4 or 2 pairs fit in the 120 registers of 544 threads (16).
-constexpr uint32_t kImmaMaxWarps = 16;
-template <uint32_t PAIRS>
-constexpr uint32_t imma_max_consumers() {
-    return PAIRS >= 8 ? 15u : 16u;
-}
+constexpr uint32_t kMaxWarps = 16;               // consumer warps (+1 producer warp)
+constexpr uint32_t kNarrowSmem = 113u * 1024u;   // (228 KB - 2 x 1 KB reserved) / 2, rounded down
+constexpr uint32_t kMaxBoxBytes = 2048;          // 256 elements of 8 bytes
+constexpr uint32_t kTileRows = 16;               // rows per tile: the M of one IMMA
+constexpr uint32_t kMaxSlots = 32;
+
+// Table entry of one block pair: 32 lanes x (w_lo, w_hi), then for each of the
+// four t (a lane's D columns 2t, 2t+1) the column scale and the two start values.
+constexpr uint32_t kPairTableBytes = 32u * 8u + 4u * 16u;
 
 struct ImmaArgs {
-    const uint8_t* w;
     const float* x;
     float* y;
     uint64_t rows;
-    uint32_t row_bytes;
+    uint32_t tiles;        // ceil(rows / 16)
     uint32_t pairs_total;  // cols / 64
-    uint32_t chunk_pairs;  // block pairs per column chunk (a multiple of 4 when chunks > 1)
-    uint32_t chunks;       // column chunks, streamed one after the other
-    uint32_t row_pitch;    // shared-memory bytes per tile row, 16 mod 32 (conflict free)
-    uint32_t warps;        // consumer warps (column slices)
+    uint32_t group_pairs;  // block pairs per column group (a multiple of seg_pairs)
+    uint32_t groups;
+    uint32_t box_bytes;    // bytes per box row = its shared-memory pitch (an odd multiple of 16)
+    uint32_t warps;        // consumer warps
+    uint32_t team;         // warps sharing a tile (a power of two dividing warps)
     uint32_t slots;
-    uint32_t slot_bytes;
+    uint32_t unit_bytes;   // 16 * box_bytes
     DeviceStatus* status;
     // Fused all-gather (npeers > 0): each finished y row is also stored at
     // peer_y[k][peer_row_offset + row] on every peer (NVLink peer stores), and
@@ -72,15 +89,36 @@ struct ImmaArgs {
     uint32_t* peer_signal[kMaxPeers];
 };
 
-constexpr uint32_t kTileRows = 16;  // rows per tile: the M of one IMMA
-
-// x limb table in shared memory: per block 144 bytes (4 limbs x 32 int8 and
-// padding that keeps the lane loads conflict free), then per block the
-// exponent e and the four limb sums.
-constexpr uint32_t kLimbBlockBytes = 144;
-
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// 2D tensor-map copy global -> this CTA's shared memory with an L2 cache hint,
+// completing on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Bounded wait until the producer has started unit `want` in a slot (false on
+// timeout, recorded in `st`, or when another warp has aborted).
+__device__ __forceinline__ bool wait_issued(volatile uint32_t* issued, uint32_t want, volatile uint32_t* abort_flag,
+                                            DeviceStatus* st, uint32_t site) {
+    if (*issued == want) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (*issued != want) {
+        if (*abort_flag != 0u) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
 
 template <uint32_t TYPE>
 struct Pair;
@@ -93,45 +131,28 @@ struct Pair<kQ4_0> {
     static constexpr uint32_t kBytes = 36, kBlock = 18;
 };
 
+// d += A * B (int8 inputs, exact int32 accumulation); A unsigned for Q4_0 nibbles.
+template <bool A_UNSIGNED>
 __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                     uint32_t b1, bool first, bool a_unsigned) {
-    if (a_unsigned) {
-        if (first)
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-        else
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-    } else {
-        if (first)
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
-                : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-        else
-            asm volatile(
-                "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-    }
+                                     uint32_t b1) {
+    if (A_UNSIGNED)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Per-lane x state for one block pair.
-struct XPair {
-    uint32_t b0[2];  // B register b0 (k < 16: even block) for the two IMMA halves; 0 unless column g is in it
-    uint32_t b1[2];  // B register b1 (k >= 16: odd block)
-    float scale;     // 2^(7*(3-lambda_b) - e_block) for this lane's D columns (2t, 2t+1)
-    int offset;      // Q4_0: 8 * (sum L_a * 128 + sum L_b) for the same columns
-};
-
-// All consumer threads: decompose x into the limb table, 8 threads per block
-// (4 positions each).  e_b makes max |x_b| * 2^e_b fall in [2^26, 2^27).
+// One 32-element block of x, 8 threads (4 positions each): the four limb
+// words of this thread's positions, the block exponent and the limb sums, all
+// written into the fragment-ordered pair table.  e_b makes max |x_b| * 2^e_b
+// fall in [2^26, 2^27).
 template <bool SUMS>
-__device__ __forceinline__ void limb_block_group(float4 v, uint32_t b, uint32_t q, bool in, uint8_t* table, int* binfo) {
+__device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, bool in, uint8_t* table) {
     float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
@@ -161,7 +182,7 @@ __device__ __forceinline__ void limb_block_group(float4 v, uint32_t b, uint32_t 
     L[2] = gather(X0 << 1, X1 << 1, X2 << 1, X3 << 1, 0x3351u) & 0x7F7F7F7Fu;
     L[1] = gather(X0 << 2, X1 << 2, X2 << 2, X3 << 2, 0x3362u) & 0x7F7F7F7Fu;
     L[0] = gather(X0 << 3, X1 << 3, X2 << 3, X3 << 3, 0x3373u);
-    int sum[4] = {0, 0, 0, 0};  // limb sums over the block (Q4_0 offsets only)
+    int sum[4] = {0, 0, 0, 0};  // limb sums over the block (Q4_0 start values only)
     if (SUMS) {
         // two sums per word: low 16 bits a non-negative sum (<= 32 * 127), high 16 bits the other
         int s32 = __dp4a(static_cast<int>(L[3]), 0x01010101, 0) + __dp4a(static_cast<int>(L[0]), 0x01010101, 0) * 65536;
@@ -178,27 +199,34 @@ __device__ __forceinline__ void limb_block_group(float4 v, uint32_t b, uint32_t 
         sum[1] = (s21 - sum[2]) >> 16;
     }
     if (in) {
-        uint32_t* tb = reinterpret_cast<uint32_t*>(table + static_cast<size_t>(b) * kLimbBlockBytes);
+        // lane (g, t) of the pair's IMMAs takes limb g & 3 of block (g >= 4 ? odd : even),
+        // positions 4t.. (w_lo) and 16+4t.. (w_hi): this thread's word is w_lo of
+        // t = q (q < 4) or w_hi of t = q - 4
+        const uint32_t odd = b & 1u;
+        uint8_t* pe = table + static_cast<size_t>(b >> 1) * kPairTableBytes;
 #pragma unroll
-        for (int l = 0; l < 4; ++l) tb[l * 8 + q] = L[l];
-        if (q == 0) {
-            int* bi = binfo + 5u * b;
-            bi[0] = e;
-            bi[1] = sum[0];
-            bi[2] = sum[1];
-            bi[3] = sum[2];
-            bi[4] = sum[3];
+        for (uint32_t l = 0; l < 4; ++l) {
+            const uint32_t lane = (4u * odd + l) * 4u + (q & 3u);
+            reinterpret_cast<uint32_t*>(pe + lane * 8u)[q >> 2] = L[l];
+        }
+        if (q < 2) {
+            // t = 2*odd + q: D columns 2t, 2t+1 = limbs la = 2q and la+1 of this block,
+            // scale 2^(7*(2-la) - e) (in [2^-126, 2^115]: a normal float)
+            const uint32_t la = 2u * q;
+            int* te = reinterpret_cast<int*>(pe + 256u + (2u * odd + q) * 16u);
+            te[0] = static_cast<int>(static_cast<uint32_t>(7 * (2 - static_cast<int>(la)) - e + 127) << 23);
+            te[1] = -8 * (q ? sum[2] : sum[0]);
+            te[2] = -8 * (q ? sum[3] : sum[1]);
         }
     }
 }
 
-// All consumer threads: decompose x into the limb table, 8 threads per block
-// (4 positions each), every x load issued before any is used.
-// e_b makes max |x_b| * 2^e_b fall in [2^26, 2^27).
+// All consumer threads: build the table of blocks [0, nblocks) of x, 8
+// threads per block, every x load issued before any is used.
 constexpr uint32_t kLimbPasses = 8;  // up to 8 * nthreads / 8 blocks staged in registers at once
 template <bool SUMS>
-__device__ __forceinline__ void build_limb_table(const float* __restrict__ x, uint32_t nblocks, uint32_t tid,
-                                                 uint32_t nthreads, uint8_t* table, int* binfo) {
+__device__ __forceinline__ void build_pair_table(const float* __restrict__ x, uint32_t nblocks, uint32_t tid,
+                                                 uint32_t nthreads, uint8_t* table) {
     const uint32_t per_pass = nthreads / 8u;
     const uint32_t q = tid & 7u;
     for (uint32_t base = 0; base < nblocks; base += per_pass * kLimbPasses) {
@@ -211,47 +239,33 @@ __device__ __forceinline__ void build_limb_table(const float* __restrict__ x, ui
 #pragma unroll
         for (uint32_t k = 0; k < kLimbPasses; ++k) {
             const uint32_t b = base + k * per_pass + tid / 8u;
-            if (base + k * per_pass < nblocks) limb_block_group<SUMS>(v[k], b, q, b < nblocks, table, binfo);
+            if (base + k * per_pass < nblocks) limb_block<SUMS>(v[k], b, q, b < nblocks, table);
         }
     }
 }
 
-// This lane's x state for block pair `gp`, read from the limb table.
-// Lane (g, t): B column n = g; g < 4 -> even block, limb g; g >= 4 -> odd block, limb g-4.
-// D columns of the lane: n = 2t, 2t+1 -> block (t >> 1), limbs 2(t&1), 2(t&1)+1.
-__device__ __forceinline__ XPair load_xpair(const uint8_t* table, const int* binfo, uint32_t gp, uint32_t lane,
-                                            bool q4) {
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    const uint32_t blk = 2u * gp + (g >= 4 ? 1u : 0u), lambda = g & 3u;
-    const uint32_t* tb = reinterpret_cast<const uint32_t*>(table + static_cast<size_t>(blk) * kLimbBlockBytes);
-    const uint32_t w_lo = tb[lambda * 8u + t], w_hi = tb[lambda * 8u + 4u + t];  // positions 4t.., 16+4t..
-    const bool even = g < 4;
-    XPair xp;
-    xp.b0[0] = even ? w_lo : 0u;
-    xp.b0[1] = even ? w_hi : 0u;
-    xp.b1[0] = even ? 0u : w_lo;
-    xp.b1[1] = even ? 0u : w_hi;
-    const uint32_t dblk = 2u * gp + (t >> 1), la = 2u * (t & 1u);
-    const int* bi = binfo + 5u * dblk;
-    const int k = 7 * (3 - static_cast<int>(la + 1u)) - bi[0];  // in [-126, 115]
-    xp.scale = __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
-    xp.offset = q4 ? 8 * (bi[1 + la] * 128 + bi[2 + la]) : 0;
-    return xp;
-}
-
-// One 16-row tile against this warp's column slice: acc0 / acc1 collect the
-// rows of fragment rows g and g+8 (this lane's D columns).  GUARD skips the
-// pairs past `valid` (the last warp of a chunk).
-template <uint32_t TYPE, uint32_t PAIRS, bool GUARD>
-__device__ __forceinline__ void tile_dot(const uint8_t* r0p, const uint8_t* r1p, const XPair (&xs)[PAIRS], uint32_t valid,
-                                         uint32_t t, uint32_t scale_blk, float& acc0, float& acc1) {
+// One segment of one tile: `valid` block pairs starting at r0p / r1p (tile
+// rows g and g+8 of the slot), their x side at pt (the pair table entries).
+// acc0 / acc1 collect rows g and g+8 (this lane's D columns).
+template <uint32_t TYPE, uint32_t SEG, bool GUARD>
+__device__ __forceinline__ void segment_dot(const uint8_t* r0p, const uint8_t* r1p, const uint8_t* pt, uint32_t valid,
+                                            uint32_t lane, uint32_t even_mask, float& acc0, float& acc1) {
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    const uint32_t t = lane & 3u;
+    const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;  // this lane's D block within a pair
 #pragma unroll
-    for (uint32_t p = 0; p < PAIRS; ++p) {
+    for (uint32_t p = 0; p < SEG; ++p) {
         if (GUARD && p >= valid) break;
-        const uint8_t* p0 = r0p + p * Pair<TYPE>::kBytes;
-        const uint8_t* p1 = r1p + p * Pair<TYPE>::kBytes;
+        const uint8_t* p0 = r0p + p * pb;
+        const uint8_t* p1 = r1p + p * pb;
+        const uint2 w = *reinterpret_cast<const uint2*>(pt + p * kPairTableBytes + lane * 8u);
+        const int4 te = *reinterpret_cast<const int4*>(pt + p * kPairTableBytes + 256u + t * 16u);
+        // B registers: column g of the block-diagonal B is in the even block (k < 16) for g < 4
+        const uint32_t b0lo = w.x & even_mask, b1lo = w.x & ~even_mask;
+        const uint32_t b0hi = w.y & even_mask, b1hi = w.y & ~even_mask;
         int d[4];
         if constexpr (TYPE == kQ8_0) {
+            d[0] = d[1] = d[2] = d[3] = 0;
 #pragma unroll
             for (uint32_t h = 0; h < 2; ++h) {
                 // even block: quant bytes 16h+4t.. at pair offset 2+16h+4t (2 mod 4)
@@ -262,9 +276,12 @@ __device__ __forceinline__ void tile_dot(const uint8_t* r0p, const uint8_t* r1p,
                 const uint32_t a2 = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
                 const uint32_t a1 = __funnelshift_r(e1[0], e1[1], 16);
                 const uint32_t a3 = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
-                imma(d, a0, a1, a2, a3, xs[p].b0[h], xs[p].b1[h], h == 0, false);
+                imma<false>(d, a0, a1, a2, a3, h ? b0hi : b0lo, h ? b1hi : b1lo);
             }
         } else {
+            // accumulators start at -8 * sum L of their column (the nibble offset)
+            d[0] = d[2] = te.y;
+            d[1] = d[3] = te.z;
             // even block quant bytes 4t.. at pair offset 2+4t; odd block at 20+4t
             const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + 4u * t);
             const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + 4u * t);
@@ -273,208 +290,224 @@ __device__ __forceinline__ void tile_dot(const uint8_t* r0p, const uint8_t* r1p,
             const uint32_t w1 = __funnelshift_r(e1[0], e1[1], 16);
             const uint32_t w3 = *reinterpret_cast<const uint32_t*>(p1 + 20u + 4u * t);
             const uint32_t m = 0x0F0F0F0Fu;
-            imma(d, w0 & m, w1 & m, w2 & m, w3 & m, xs[p].b0[0], xs[p].b1[0], true, true);
-            imma(d, (w0 >> 4) & m, (w1 >> 4) & m, (w2 >> 4) & m, (w3 >> 4) & m, xs[p].b0[1], xs[p].b1[1],
-                 false, true);
+            imma<true>(d, w0 & m, w1 & m, w2 & m, w3 & m, b0lo, b1lo);
+            imma<true>(d, (w0 >> 4) & m, (w1 >> 4) & m, (w2 >> 4) & m, (w3 >> 4) & m, b0hi, b1hi);
         }
         // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
-        const int v0 = d[0] * 128 + d[1] - xs[p].offset;
-        const int v1 = d[2] * 128 + d[3] - xs[p].offset;
-        const float s0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk)) * xs[p].scale;
-        const float s1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk)) * xs[p].scale;
+        const float xs = __int_as_float(te.x);
+        const int v0 = d[0] * 128 + d[1];
+        const int v1 = d[2] * 128 + d[3];
+        const float s0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk)) * xs;
+        const float s1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk)) * xs;
         acc0 = fmaf(static_cast<float>(v0), s0, acc0);
         acc1 = fmaf(static_cast<float>(v1), s1, acc1);
     }
 }
 
-// MULTI: the rows are cut into more than one column chunk.
-template <uint32_t TYPE, uint32_t PAIRS, bool MULTI>
-__global__ void __launch_bounds__((imma_max_consumers<PAIRS>() + 1) * 32, 1) gemv_imma_kernel(const ImmaArgs a) {
+// MULTI: the rows are cut into more than one column group.  SEG: block pairs
+// per unit.
+template <uint32_t TYPE, uint32_t SEG, bool MULTI>
+// At most 96 registers: registers are charged per group of four warps, so a
+// CTA of 17 warps is charged as 20 (20 x 32 x 96 = 61440 of 65536).
+__global__ void __maxnreg__(96)
+    gemv_imma_kernel(const __grid_constant__ CUtensorMap map, const ImmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t S = a.slots, W = a.warps;
-    const uint32_t table_blocks = 2u * a.chunk_pairs;  // limb table capacity (one chunk)
-    // [ring: S slots][limb table][block info][barriers][partial sums][abort flag]
-    uint8_t* table = smem + static_cast<size_t>(S) * a.slot_bytes;
-    int* binfo = reinterpret_cast<int*>(table + static_cast<size_t>(table_blocks) * kLimbBlockBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(
-        reinterpret_cast<uint8_t*>(binfo) + ((static_cast<size_t>(table_blocks) * 20u + 7u) & ~static_cast<size_t>(7)));
+    // [ring: S units][pair table][full S][empty S][team 8][issued S][team partial sums 2 x W x 16][abort flag]
+    uint8_t* table = smem + static_cast<size_t>(S) * a.unit_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(table + static_cast<size_t>(a.group_pairs) * kPairTableBytes);
     uint64_t* empty = full + S;
-    uint64_t* redbar = empty + S;
-    float* red = reinterpret_cast<float*>(redbar + S);  // [S][W][16]
-    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(red + static_cast<size_t>(S) * W * 16u);
+    // issued[s]: the unit whose copy into slot s was last started.  A warp skips
+    // the units of other warps, so it may reach a slot two or more uses ahead of
+    // its barrier's phase, which a parity wait cannot tell apart; it first waits
+    // for its own unit to be issued into the slot (then the barrier's phase is
+    // that unit's).
+    uint64_t* teambar = empty + S;  // [8]: a team's partial sums are complete (K arrivals)
+    volatile uint32_t* issued = reinterpret_cast<volatile uint32_t*>(teambar + 8);
+    float* red = reinterpret_cast<float*>(const_cast<uint32_t*>(issued) + S);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(red + 2u * W * 16u);
 
-    // this CTA's rows: an even split of all rows (to one row), cut into 16-row tiles;
-    // the unit of work is (column chunk c, tile j), chunk-major
-    const uint64_t row_begin = a.rows * blockIdx.x / gridDim.x;
-    const uint64_t row_end = a.rows * (blockIdx.x + 1) / gridDim.x;
-    const uint32_t my_tiles = static_cast<uint32_t>((row_end - row_begin + kTileRows - 1) / kTileRows);
-    const uint32_t nchunks = MULTI ? a.chunks : 1u;
-    const uint32_t units = my_tiles * nchunks;
+    // this CTA's tiles: an even split of all 16-row tiles
+    const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * blockIdx.x / gridDim.x);
+    const uint32_t tile_end = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t my_tiles = tile_end - tile_begin;
+    const uint32_t ngroups = MULTI ? a.groups : 1u;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], W);
-            mbar_init(&redbar[s], W);
+            mbar_init(&empty[s], 1);
+            issued[s] = 0xFFFFFFFFu;
         }
+        for (uint32_t i = 0; i < 8; ++i) mbar_init(&teambar[i], a.team);
         *abort_flag = 0u;
         fence_barrier_init();
     }
     __syncthreads();
+    // The next kernel on the stream may be scheduled now: its CTAs only stream
+    // their weights until this grid has completed.
+    grid_launch_dependents();
 
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    const uint32_t teams = W / a.team;
     if (warp == W) {
-        // ---------------- producer ----------------
-        // Lane r copies row r's chunk (the whole row when there is one chunk)
-        // into its padded shared-memory row: 16 copies issued in parallel.
+        // ---------------- producer: one thread ----------------
+        // The weights are not written by the previous kernel on the stream, so
+        // they are streamed before its completion (griddepcontrol.wait is only
+        // needed for x).  Units in order: group, block of `teams` tiles (one per
+        // team), segment, tile -- so the ring always spans every warp's work.
+        if (lane != 0) return;
         const uint64_t policy = l2_policy_evict_first();
         uint32_t slot = 0, use = 0, u = 0;
-        for (; u < units; ++u) {
-            bool ok = true;
-            if (lane == 0 && use > 0) ok = mbar_wait_bounded(&empty[slot], (use - 1u) & 1u, a.status, 11u);
-            if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) {
-                if (lane == 0) *abort_flag = 1u;
-                break;
-            }
-            const uint32_t c = u / my_tiles, j = u - c * my_tiles;
-            const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * kTileRows;
-            const uint64_t left = row_end - row0;
-            const uint32_t nrows = left < kTileRows ? static_cast<uint32_t>(left) : kTileRows;
-            uint8_t* dst = smem + static_cast<size_t>(slot) * a.slot_bytes;
-            const uint32_t pair0 = c * a.chunk_pairs;
-            const uint32_t cp = a.pairs_total - pair0 < a.chunk_pairs ? a.pairs_total - pair0 : a.chunk_pairs;
-            const uint32_t cbytes = cp * Pair<TYPE>::kBytes, cofs = pair0 * Pair<TYPE>::kBytes;
-            if (lane == 0) mbar_arrive_expect_tx(&full[slot], nrows * cbytes);
-            __syncwarp();
-            if (lane < nrows)
-                bulk_copy_g2s(dst + static_cast<size_t>(lane) * a.row_pitch, a.w + (row0 + lane) * a.row_bytes + cofs,
-                              cbytes, &full[slot], policy);
-            if (++slot == S) {
-                slot = 0;
-                ++use;
-            }
-        }
-        // drain: every issued copy must land before the CTA may exit
-        if (lane == 0) {
-            const uint32_t first = u > S ? u - S : 0;
-            for (uint32_t k = first; k < u; ++k) mbar_wait_bounded(&full[k % S], (k / S) & 1u, a.status, 12u);
-        }
-        return;
-    }
-
-    // ---------------- consumers: warp w owns block pairs [w*PAIRS, (w+1)*PAIRS) of each chunk ----------------
-    constexpr bool kQ4 = TYPE == kQ4_0;
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;  // this lane's D block within a pair
-    const size_t col0 = static_cast<size_t>(warp) * PAIRS * Pair<TYPE>::kBytes;
-    // fragment rows g and g+8 = tile rows g and g+8
-    const size_t off_a = static_cast<size_t>(g) * a.row_pitch + col0;
-    const size_t off_b = off_a + 8u * static_cast<size_t>(a.row_pitch);
-
-    grid_dependency_wait();  // x may come from the previous kernel
-    bool ok = true;
-    uint32_t slot = 0, parity = 0, u = 0;
-    for (uint32_t c = 0; c < nchunks; ++c) {
-        const uint32_t pair0 = c * a.chunk_pairs;
-        const uint32_t cp = a.pairs_total - pair0 < a.chunk_pairs ? a.pairs_total - pair0 : a.chunk_pairs;
-        if (c > 0) named_barrier_sync(1, W * 32u);  // every warp has its x registers of chunk c-1
-        build_limb_table<kQ4>(a.x + static_cast<size_t>(pair0) * 64u, 2u * cp, threadIdx.x, W * 32u, table, binfo);
-        named_barrier_sync(1, W * 32u);
-        const uint32_t pw = warp * PAIRS;
-        const uint32_t valid = cp > pw ? (cp - pw < PAIRS ? cp - pw : PAIRS) : 0u;  // warp-uniform
-        XPair xs[PAIRS];
-#pragma unroll
-        for (uint32_t p = 0; p < PAIRS; ++p) {
-            if (p < valid) {
-                xs[p] = load_xpair(table, binfo, pw + p, lane, kQ4);
-            } else {
-                xs[p].b0[0] = xs[p].b0[1] = xs[p].b1[0] = xs[p].b1[1] = 0u;
-                xs[p].scale = 0.f;
-                xs[p].offset = 0;
-            }
-        }
-        if (c == 0) grid_launch_dependents();
-
-        for (uint32_t j = 0; j < my_tiles; ++j, ++u) {
-            if (ok && *abort_flag != 0u) ok = false;
-            if (ok && !mbar_wait_bounded(&full[slot], parity, a.status, 13u)) {
-                ok = false;
-                *abort_flag = 1u;
-            }
-            if (ok) {
-                const uint8_t* tile = smem + static_cast<size_t>(slot) * a.slot_bytes;
-                const uint8_t* r0p = tile + off_a;
-                const uint8_t* r1p = tile + off_b;
-                float acc0 = 0.f, acc1 = 0.f;
-                if (valid == PAIRS)  // every pair of the slice exists: no per-pair checks
-                    tile_dot<TYPE, PAIRS, false>(r0p, r1p, xs, valid, t, scale_blk, acc0, acc1);
-                else
-                    tile_dot<TYPE, PAIRS, true>(r0p, r1p, xs, valid, t, scale_blk, acc0, acc1);
-                // fold the four t-lanes (columns) of each row
-                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
-                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
-                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
-                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
-                float* rs = red + (static_cast<size_t>(slot) * W + warp) * 16u;
-                if (t == 0) {
-                    rs[g] = acc0;
-                    rs[g + 8] = acc1;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&redbar[slot]);
-                if (warp != 0) {
-                    if (lane == 0) mbar_arrive(&empty[slot]);
-                } else {
-                    // warp 0 folds the column slices of every row in fixed order; chunks
-                    // add up in y in chunk order (only this thread touches the row)
-                    if (!mbar_wait_bounded(&redbar[slot], parity, a.status, 14u)) {
-                        ok = false;
+        bool ok = true;
+        for (uint32_t gi = 0; gi < ngroups && ok; ++gi) {
+            const uint32_t pair_g = gi * a.group_pairs;
+            const uint32_t gp = a.pairs_total - pair_g < a.group_pairs ? a.pairs_total - pair_g : a.group_pairs;
+            const uint32_t nseg = (gp + SEG - 1u) / SEG;
+            for (uint32_t tb = 0; tb < my_tiles && ok; tb += teams)
+            for (uint32_t s = 0; s < nseg && ok; ++s) {
+                const uint32_t nb = my_tiles - tb < teams ? my_tiles - tb : teams;
+                for (uint32_t jj = 0; jj < nb; ++jj, ++u) {
+                    const int32_t row0 = static_cast<int32_t>((tile_begin + tb + jj) * kTileRows);
+                    if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1u) & 1u, a.status, 11u)) {
                         *abort_flag = 1u;
-                    } else {
-                        const uint64_t row0 = row_begin + static_cast<uint64_t>(j) * kTileRows;
-                        if (lane < kTileRows && row0 + lane < row_end) {
-                            const float* rr = red + static_cast<size_t>(slot) * W * 16u + lane;
-                            float v = 0.f;
-                            for (uint32_t k = 0; k < W; ++k) v += rr[k * 16u];
-                            if (MULTI && c > 0) v += a.y[row0 + lane];
-                            a.y[row0 + lane] = v;
-                        }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&empty[slot]);
+                        ok = false;
+                        break;
+                    }
+                    // the previous use of the slot is consumed: full[slot] is in this unit's phase
+                    issued[slot] = u;
+                    mbar_arrive_expect_tx(&full[slot], a.unit_bytes);
+                    // x in 8-byte elements: pair_g and SEG are multiples of 4, so the byte
+                    // offset is a multiple of 16
+                    const int32_t x0 = static_cast<int32_t>((pair_g + s * SEG) * pb / 8u);
+                    tma_load_2d_hint(smem_addr(smem + static_cast<size_t>(slot) * a.unit_bytes), &map, x0, row0,
+                                     &full[slot], policy);
+                    if (++slot == S) {
+                        slot = 0;
+                        ++use;
                     }
                 }
             }
-            if (++slot == S) {
-                slot = 0;
-                parity ^= 1u;
-            }
         }
+        // drain: every issued copy must land before the CTA may exit
+        const uint32_t first = u > S ? u - S : 0;
+        for (uint32_t k = first; k < u; ++k) mbar_wait_bounded(&full[k % S], (k / S) & 1u, a.status, 12u);
+        return;
     }
-    if (a.npeers != 0u && warp == 0 && ok) {
-        // This CTA's rows, all written by warp 0, go to every peer as coalesced
-        // stores off the tile pipeline; then lane 0 publishes the CTA on each
-        // peer with a system-scope release add (ordered after the whole warp's
-        // stores by the warp barrier).
-        __syncwarp();
-        for (uint64_t r = row_begin + lane; r < row_end; r += 32u) {
-            const float v = __ldcg(a.y + r);
-            for (uint32_t k = 0; k < a.npeers; ++k) a.peer_y[k][a.peer_row_offset + r] = v;
+
+    // ---------------- consumers ----------------
+    // Teams of K warps: team i owns tiles i, i + W/K, ...; member k of a team
+    // runs segments k, k + K, ... of each of them (K = 1: a warp owns whole tiles).
+    constexpr bool kQ4 = TYPE == kQ4_0;
+    const uint32_t K = a.team, team = warp / K, member = warp - team * K;
+    const uint32_t g = lane >> 2;
+    const uint32_t even_mask = g < 4 ? 0xFFFFFFFFu : 0u;
+    // fragment rows g and g+8 = unit rows g and g+8
+    const size_t off_a = static_cast<size_t>(g) * a.box_bytes;
+    const size_t off_b = off_a + 8u * static_cast<size_t>(a.box_bytes);
+
+    grid_dependency_wait();  // x may come from the previous kernel
+    bool ok = true;
+    uint32_t u = 0;      // first unit of the group, counted like the producer
+    uint32_t round = 0;  // tiles this team has finished, over all groups (team barrier phase)
+    for (uint32_t gi = 0; gi < ngroups; ++gi) {
+        const uint32_t pair_g = gi * a.group_pairs;
+        const uint32_t gp = a.pairs_total - pair_g < a.group_pairs ? a.pairs_total - pair_g : a.group_pairs;
+        const uint32_t nseg = (gp + SEG - 1u) / SEG;
+        if (gi > 0) named_barrier_sync(1, W * 32u);  // every warp is done with the last group's table
+        build_pair_table<kQ4>(a.x + static_cast<size_t>(pair_g) * 64u, 2u * gp, threadIdx.x, W * 32u, table);
+        named_barrier_sync(1, W * 32u);
+        for (uint32_t tb = 0; tb < my_tiles; tb += teams) {
+            const uint32_t j = tb + team;
+            if (j >= my_tiles) break;  // the last block has fewer tiles than teams
+            const uint32_t nb = my_tiles - tb < teams ? my_tiles - tb : teams;
+            float acc0 = 0.f, acc1 = 0.f;
+            for (uint32_t s = member; s < nseg; s += K) {
+                const uint32_t uj = u + tb * nseg + s * nb + team;
+                const uint32_t slot = uj % S, parity = (uj / S) & 1u;
+                if (ok && *abort_flag != 0u) ok = false;
+                if (ok && !(wait_issued(&issued[slot], uj, abort_flag, a.status, 15u) &&
+                            mbar_wait_bounded(&full[slot], parity, a.status, 13u))) {
+                    ok = false;
+                    *abort_flag = 1u;
+                }
+                if (ok) {
+                    const uint8_t* unit = smem + static_cast<size_t>(slot) * a.unit_bytes;
+                    const uint32_t left = gp - s * SEG;
+                    const uint8_t* pt = table + static_cast<size_t>(s) * SEG * kPairTableBytes;
+                    if (left >= SEG)
+                        segment_dot<TYPE, SEG, false>(unit + off_a, unit + off_b, pt, SEG, lane, even_mask, acc0, acc1);
+                    else
+                        segment_dot<TYPE, SEG, true>(unit + off_a, unit + off_b, pt, left, lane, even_mask, acc0, acc1);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                }
+            }
+            // fold the four t-lanes (columns) of each row
+            acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+            acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+            // row r of the tile: acc0 (r < 8) or acc1 (r >= 8) of lane 4 (r mod 8); lane r takes it
+            const uint32_t r = lane & 15u;
+            const float v0 = __shfl_sync(0xFFFFFFFFu, acc0, 4u * (r & 7u));
+            const float v1 = __shfl_sync(0xFFFFFFFFu, acc1, 4u * (r & 7u));
+            float v = r < 8 ? v0 : v1;
+            if (K > 1) {
+                // the team's partial sums meet in shared memory (two buffers by tile parity);
+                // member 0 adds them up in member order
+                float* rb = red + (static_cast<size_t>(2u * team + (round & 1u)) * K) * 16u;
+                if (lane < 16) rb[member * 16u + lane] = v;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&teambar[team]);
+                // every member waits (no member can arrive for the next round before this
+                // round is complete, so the parity is unambiguous); member 0 adds up
+                if (!mbar_wait_bounded(&teambar[team], round & 1u, a.status, 16u)) {
+                    ok = false;
+                    *abort_flag = 1u;
+                }
+                if (member == 0) {
+                    v = rb[lane & 15u];
+                    for (uint32_t k = 1; k < K; ++k) v += rb[k * 16u + (lane & 15u)];
+                }
+            }
+            if (ok && member == 0 && lane < 16) {
+                const uint64_t row = static_cast<uint64_t>(tile_begin + j) * kTileRows + lane;
+                if (row < a.rows) {
+                    if (MULTI && gi > 0) v += a.y[row];  // groups add up in group order
+                    a.y[row] = v;
+                    if (a.npeers != 0u && gi + 1u == ngroups)
+                        for (uint32_t k = 0; k < a.npeers; ++k) a.peer_y[k][a.peer_row_offset + row] = v;
+                }
+            }
+            ++round;
         }
-        __syncwarp();
-        if (lane == 0)
+        u += my_tiles * nseg;
+    }
+    if (a.npeers != 0u) {
+        // every warp's peer stores are visible system-wide before the CTA is
+        // published on each peer with a release add
+        __threadfence_system();
+        named_barrier_sync(1, W * 32u);
+        if (warp == 0 && lane == 0 && *abort_flag == 0u)
             for (uint32_t k = 0; k < a.npeers; ++k)
                 asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_signal[k]) : "memory");
     }
 }
 
-template <uint32_t TYPE, uint32_t PAIRS, bool MULTI>
-cudaError_t launch_imma_t(const ImmaPlan& plan, const ImmaArgs& args, cudaStream_t stream, bool pdl) {
+template <uint32_t TYPE, uint32_t SEG, bool MULTI>
+cudaError_t launch_imma_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                          bool pdl) {
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_imma_kernel<TYPE, PAIRS, MULTI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
+        auto k = gemv_imma_kernel<TYPE, SEG, MULTI>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        // the whole unified L1 as shared memory, so two 113 KB CTAs fit on an SM
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
@@ -488,23 +521,33 @@ cudaError_t launch_imma_t(const ImmaPlan& plan, const ImmaArgs& args, cudaStream
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, PAIRS, MULTI>, args);
+    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, SEG, MULTI>, map, args);
 }
 
 template <uint32_t TYPE>
-cudaError_t launch_imma_p(const ImmaPlan& plan, const ImmaArgs& args, cudaStream_t stream, bool pdl) {
-    switch (plan.pairs) {
-        case 2: return plan.chunks > 1 ? launch_imma_t<TYPE, 2, true>(plan, args, stream, pdl)
-                                       : launch_imma_t<TYPE, 2, false>(plan, args, stream, pdl);
-        case 4: return plan.chunks > 1 ? launch_imma_t<TYPE, 4, true>(plan, args, stream, pdl)
-                                       : launch_imma_t<TYPE, 4, false>(plan, args, stream, pdl);
-        case 8: return plan.chunks > 1 ? launch_imma_t<TYPE, 8, true>(plan, args, stream, pdl)
-                                       : launch_imma_t<TYPE, 8, false>(plan, args, stream, pdl);
+cudaError_t launch_imma_p(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                          bool pdl) {
+    const bool multi = plan.groups > 1;
+    switch (plan.seg_pairs) {
+        case 4: return multi ? launch_imma_t<TYPE, 4, true>(plan, map, args, stream, pdl)
+                             : launch_imma_t<TYPE, 4, false>(plan, map, args, stream, pdl);
+        case 8: return multi ? launch_imma_t<TYPE, 8, true>(plan, map, args, stream, pdl)
+                             : launch_imma_t<TYPE, 8, false>(plan, map, args, stream, pdl);
+        case 16: return multi ? launch_imma_t<TYPE, 16, true>(plan, map, args, stream, pdl)
+                              : launch_imma_t<TYPE, 16, false>(plan, map, args, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
 uint64_t align_up64(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+// Bytes of one box row of `bp` block pairs: the data rounded to an odd
+// multiple of 16 bytes (the eight fragment rows of a load then fall in
+// distinct 16-byte bank groups).
+uint64_t box_row_bytes(uint64_t bp, uint64_t pair_bytes) {
+    const uint64_t b = align_up64(bp * pair_bytes, 16);
+    return (b / 16u) % 2u == 0 ? b + 16u : b;
+}
 
 }  // namespace
 
@@ -512,104 +555,82 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
                    const ImmaTuning* tune) {
     ImmaPlan p;
     if (type != kQ8_0 && type != kQ4_0) return p;
-    if (cols % 64u || cols > 0xFFFFFFFFull || rows == 0 || rows > 0xFFFFFFFFull || num_sms <= 0) return p;
+    // tensor-map coordinates are int32: rows below 2^31
+    if (cols % 64u || cols > 0xFFFFFFFFull || rows == 0 || rows >= 0x80000000ull || num_sms <= 0) return p;
     const uint64_t rb = row_bytes_of(type, cols);
-    if (rb % 16u) return p;
+    if (rb % 16u) return p;  // the tensor map's row stride
     const uint64_t pair_bytes = type == kQ8_0 ? 68u : 36u;
     const uint64_t pairs_total = cols / 64u;
     const ImmaTuning t = tune ? *tune : ImmaTuning{};
-    // Column chunks: at most 15 warps x 8 pairs of x limbs live in registers at a
-    // time.  Longer rows are cut into chunks of a multiple of 4 pairs (so every
-    // chunk starts on a 16-byte boundary), streamed one after the other; more
-    // chunks than that minimum when a chunk's 16-row tile would leave fewer than
-    // 3 ring slots.
-    constexpr uint64_t kMaxChunkPairs = 15u * 8u;
-    uint64_t budget = t.smem_budget ? t.smem_budget : static_cast<uint64_t>(max_smem_optin);
+    const uint64_t tiles = (rows + kTileRows - 1) / kTileRows;
+    // One CTA per SM per launch, sized so two fit on an SM (the next launch's
+    // CTA beside it) unless a deeper ring is asked for.
+    const bool wide = t.wide != 0;
+    uint64_t budget = wide ? static_cast<uint64_t>(max_smem_optin) : kNarrowSmem;
+    if (t.smem_budget && t.smem_budget < budget) budget = t.smem_budget;
     if (budget > static_cast<uint64_t>(max_smem_optin)) budget = max_smem_optin;
-    const uint32_t grid = static_cast<uint32_t>(rows < static_cast<uint64_t>(num_sms) ? rows : num_sms);
-    const uint64_t rows_per_cta = (rows + grid - 1) / grid;
-    const uint64_t tiles_per_cta = (rows_per_cta + kTileRows - 1) / kTileRows;
-
-    struct Cand {
-        bool ok = false;
-        uint64_t chunks = 0, chunk_pairs = 0, pitch = 0, slot_bytes = 0, slots = 0, smem = 0;
-        uint32_t pairs = 0, warps = 0;
-    };
-    auto evaluate = [&](uint64_t chunks) {
-        Cand c;
-        uint64_t cpairs = pairs_total;
-        if (chunks > 1) {
-            if (pairs_total % 4u) return c;
-            cpairs = align_up64((pairs_total + chunks - 1) / chunks, 4);
-            if ((pairs_total + cpairs - 1) / cpairs != chunks) return c;
-        }
-        if (cpairs > kMaxChunkPairs) return c;
-        // pairs per warp in {8, 4, 2}: the most pairs per warp (more independent
-        // IMMA chains per warp) that still leaves at least 8 consumer warps, else
-        // the most warps; 8 pairs allow 15 warps, fewer pairs 16.  The last warp
-        // may own fewer pairs.
-        for (uint32_t pp : {8u, 4u, 2u}) {
-            const uint64_t w = (cpairs + pp - 1) / pp;
-            if (w > (pp >= 8 ? 15u : kImmaMaxWarps)) continue;
-            if (t.warps && w != t.warps) continue;
-            if (c.warps == 0 || (c.warps < 8 && w > c.warps)) {
-                c.pairs = pp;
-                c.warps = static_cast<uint32_t>(w);
-            }
-        }
-        if (c.warps == 0) return c;
-        // one bulk copy per tile row (its chunk) into a row of pitch 16 mod 32
-        // bytes, so the eight fragment rows of a load sit in distinct banks
-        // (copying two rows per copy into 2-row groups measured no faster)
-        const uint64_t cbytes = cpairs * pair_bytes;
-        c.pitch = (cbytes % 32u == 16u) ? cbytes : cbytes + 16u;
-        c.slot_bytes = align_up64(kTileRows * c.pitch, 128);
-        const uint64_t table_blocks = 2u * cpairs;
-        const uint64_t fixed = table_blocks * kLimbBlockBytes + align_up64(table_blocks * 20u, 8) + 16u;
-        auto smem_of = [&](uint64_t s) { return s * c.slot_bytes + fixed + 24u * s + 4ull * s * c.warps * 16u; };
-        // enough slots to hold a CTA's whole work when it fits, else the most that fit (>= 2)
-        uint64_t slots = t.slots ? t.slots : tiles_per_cta * chunks;
-        if (slots < 2) slots = 2;
-        if (slots > 8) slots = 8;
-        while (slots > 2 && smem_of(slots) > budget) --slots;
-        if (smem_of(slots) > budget) return c;
-        c.chunks = chunks;
-        c.chunk_pairs = cpairs;
-        c.slots = slots;
-        c.smem = smem_of(slots);
-        c.ok = true;
-        return c;
-    };
-    const uint64_t c_min = (pairs_total + kMaxChunkPairs - 1) / kMaxChunkPairs;
-    Cand best;
-    for (uint64_t chunks = c_min; chunks <= c_min + 8 && chunks <= pairs_total; ++chunks) {
-        const Cand c = evaluate(chunks);
-        if (!c.ok) continue;
-        if (!best.ok || (best.slots < 3 && c.slots > best.slots)) best = c;
-        if (best.slots >= 3 || best.slots >= tiles_per_cta * best.chunks) break;
+    const uint64_t per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1u;
+    const uint64_t grid = tiles < per_sm * num_sms ? tiles : per_sm * num_sms;
+    const uint64_t tiles_per_cta = (tiles + grid - 1) / grid;
+    // unit: 16 rows x 16 block pairs (Q4_0, 9.5 KB) or 8 (Q8_0, 9 KB), halved
+    // (down to 4) while a CTA would have fewer units than warps
+    uint64_t seg = t.seg_pairs ? t.seg_pairs : (type == kQ4_0 ? 16u : 8u);
+    if (seg != 4u && seg != 8u && seg != 16u) return p;
+    while (!t.seg_pairs && seg > 4u && (seg > pairs_total || tiles_per_cta * ((pairs_total + seg - 1) / seg) < kMaxWarps))
+        seg /= 2u;
+    const uint64_t box_bytes = box_row_bytes(seg, pair_bytes);
+    if (box_bytes > kMaxBoxBytes) return p;
+    const uint64_t unit_bytes = kTileRows * box_bytes;  // a multiple of 256
+    // column group: the whole row when its table fits the table budget, else a
+    // multiple of the segment
+    const uint64_t table_budget = t.table_budget ? t.table_budget : 24u * 1024u;
+    uint64_t group = align_up64(pairs_total, seg);
+    if (group * kPairTableBytes > table_budget) {
+        group = (table_budget / kPairTableBytes) / seg * seg;
+        if (group == 0) group = seg;
     }
-    if (!best.ok) return p;
-    const uint64_t chunks = best.chunks, chunk_pairs = best.chunk_pairs, pitch = best.pitch;
-    const uint64_t slots = best.slots, slot_bytes = best.slot_bytes;
-    const uint32_t pairs = best.pairs, warps = best.warps;
+    const uint64_t groups = (pairs_total + group - 1) / group;
+    // Teams: a CTA with fewer tiles than warps lets 2, 4 or 8 warps share a tile
+    // (each a share of its segments) so that up to 8 warps stay busy.
+    const uint64_t nseg = (group + seg - 1) / seg;
+    // Team size K: the smallest power of two (at most the segments per tile)
+    // that gives every warp a share, tiles x K >= warps.
+    uint64_t team = 1;
+    while (team * 2u <= nseg && team * 2u <= kMaxWarps && tiles_per_cta * team < kMaxWarps) team *= 2u;
+    const uint64_t nteams = tiles_per_cta < kMaxWarps / team ? tiles_per_cta : kMaxWarps / team;
+    const uint64_t warps = nteams * team;
+    // table, 8 team barriers, partial sums, abort flag
+    const uint64_t fixed = group * kPairTableBytes + 64u + 2u * warps * 16u * 4u + 16u;
+    auto smem_of = [&](uint64_t s) { return s * unit_bytes + fixed + 20u * s; };
+    // ring: the CTA's whole work when it fits, else the most slots that fit
+    const uint64_t work = tiles_per_cta * groups * nseg;
+    uint64_t slots = t.slots ? t.slots : work;
+    if (slots < 2) slots = 2;
+    if (slots > kMaxSlots) slots = kMaxSlots;
+    while (slots > 2 && smem_of(slots) > budget) --slots;
+    if (smem_of(slots) > budget) return p;
     p.type = type;
-    p.warps = warps;
-    p.pairs = pairs;
+    p.wide = wide;
+    p.warps = static_cast<uint32_t>(warps);
+    p.team = static_cast<uint32_t>(team);
+    p.seg_pairs = static_cast<uint32_t>(seg);
     p.tile_rows = kTileRows;
-    p.row_stride = static_cast<uint32_t>(pitch);
-    p.tiles = static_cast<uint32_t>((rows + kTileRows - 1) / kTileRows);
+    p.tiles = static_cast<uint32_t>(tiles);
     p.slots = static_cast<uint32_t>(slots);
-    p.slot_bytes = static_cast<uint32_t>(slot_bytes);
-    p.grid = grid;
-    p.smem_bytes = static_cast<uint32_t>(best.smem);
-    p.chunks = static_cast<uint32_t>(chunks);
-    p.chunk_pairs = static_cast<uint32_t>(chunk_pairs);
+    p.unit_bytes = static_cast<uint32_t>(unit_bytes);
+    p.box_bytes = static_cast<uint32_t>(box_bytes);
+    p.grid = static_cast<uint32_t>(grid);
+    p.smem_bytes = static_cast<uint32_t>(smem_of(slots));
+    p.groups = static_cast<uint32_t>(groups);
+    p.group_pairs = static_cast<uint32_t>(group);
     p.ok = true;
     return p;
 }
 
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather) {
+    if (!plan.ok || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+        return cudaErrorInvalidValue;
     ImmaArgs a{};
     if (gather != nullptr) {
         if (gather->npeers > kMaxPeers) return cudaErrorInvalidValue;
@@ -620,21 +641,32 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
             a.peer_signal[k] = gather->peer_signal[k];
         }
     }
-    a.w = static_cast<const uint8_t*>(w);
+    const uint64_t rb = row_bytes_of(plan.type, cols);
+    // The weight as rows of 8-byte elements; a box is 16 rows x box_bytes.
+    EncodeTiled enc = encode_tiled_fn();
+    if (enc == nullptr) return cudaErrorNotSupported;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {rb / 8u, rows}, strides[1] = {rb};
+    const cuuint32_t box[2] = {plan.box_bytes / 8u, kTileRows}, es[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
     a.x = x;
     a.y = y;
     a.rows = rows;
-    a.row_bytes = static_cast<uint32_t>(row_bytes_of(plan.type, cols));
+    a.tiles = plan.tiles;
     a.pairs_total = static_cast<uint32_t>(cols / 64u);
-    a.chunk_pairs = plan.chunk_pairs;
-    a.chunks = plan.chunks;
-    a.row_pitch = plan.row_stride;
+    a.group_pairs = plan.group_pairs;
+    a.groups = plan.groups;
+    a.box_bytes = plan.box_bytes;
     a.warps = plan.warps;
+    a.team = plan.team;
     a.slots = plan.slots;
-    a.slot_bytes = plan.slot_bytes;
+    a.unit_bytes = plan.unit_bytes;
     a.status = status;
-    if (plan.type == kQ8_0) return launch_imma_p<kQ8_0>(plan, a, stream, pdl);
-    return launch_imma_p<kQ4_0>(plan, a, stream, pdl);
+    if (plan.type == kQ8_0) return launch_imma_p<kQ8_0>(plan, map, a, stream, pdl);
+    return launch_imma_p<kQ4_0>(plan, map, a, stream, pdl);
 }
 
 }  // namespace nedo_gpu

@@ -1,6 +1,7 @@
 // launch.h -- host-side launchers of the matvec kernels (internal to libnedo_gpu.so).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -54,28 +55,33 @@ cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, 
                           cudaStream_t stream, bool pdl);
 
 // Batch-1 Q8_0 / Q4_0 on the int8 tensor pipe (mma.sync m16n8k32, x as exact
-// int8 limbs).  16-row tiles, each warp a fixed column slice of a column
-// chunk; rows longer than one chunk are streamed chunk after chunk.
+// int8 limbs).  A unit of work is 16 rows x seg_pairs block pairs, one
+// tensor-map copy; each consumer warp owns whole 16-row tiles.
 struct ImmaPlan {
     bool ok = false;
+    bool wide = false;         // ring sized for the whole SM (else two CTAs fit on an SM)
     uint32_t type = 0;
-    uint32_t warps = 0;        // consumer warps (column slices); one more warp streams tiles
-    uint32_t pairs = 0;        // block pairs per warp
+    uint32_t warps = 0;        // consumer warps; one more warp streams units
+    uint32_t team = 0;         // warps sharing one tile (its segments split among them)
+    uint32_t seg_pairs = 0;    // block pairs per unit
     uint32_t tile_rows = 0;    // 16
-    uint32_t row_stride = 0;   // shared-memory pitch of one tile row (16 mod 32 bytes)
-    uint32_t tiles = 0;
+    uint32_t tiles = 0;        // ceil(rows / 16)
     uint32_t slots = 0;
-    uint32_t slot_bytes = 0;
+    uint32_t unit_bytes = 0;   // shared-memory bytes per slot
+    uint32_t box_bytes = 0;    // bytes per unit row: its pitch (an odd multiple of 16)
     uint32_t smem_bytes = 0;
     uint32_t grid = 0;
-    uint32_t chunks = 0;       // column chunks per row
-    uint32_t chunk_pairs = 0;  // block pairs per chunk
+    uint32_t groups = 0;       // column groups per row (the x table is rebuilt between them)
+    uint32_t group_pairs = 0;  // block pairs per group
 };
 
 struct ImmaTuning {
-    uint32_t warps = 0;
+    int wide = -1;             // 1 = ring sized for the whole SM
+    uint32_t ctas_per_sm = 0;  // grid = SMs x this (at most the tile count)
     uint32_t slots = 0;
+    uint32_t seg_pairs = 0;    // 8 or 16
     uint32_t smem_budget = 0;
+    uint32_t table_budget = 0; // bytes of x table built at once (0 = default)
 };
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
@@ -122,5 +128,12 @@ cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float
                            uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream);
 
 uint64_t row_bytes_of(uint32_t type, uint64_t cols);
+
+// cuTensorMapEncodeTiled reached through the runtime's driver entry point
+// (null when the driver does not provide it).
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled_fn();
 
 }  // namespace nedo_gpu

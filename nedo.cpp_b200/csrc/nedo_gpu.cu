@@ -554,7 +554,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             out[3] = ip.smem_bytes;
             out[4] = ip.tile_rows;
             out[5] = ip.slots;
-            out[6] = ip.slot_bytes;
+            out[6] = ip.unit_bytes;
             out[7] = ip.warps;
             return 0;
         }
