@@ -89,12 +89,12 @@ def sweep_bytes(wl, batch):
     """Algorithmic bytes of one step: every weight once, x and y per token."""
     return sum(r * B.row_bytes(t, c) + batch * 4 * (r + c) for _, t, r, c in sweep_matrices(wl))
 
-# DRAM bytes (read + write) per launch of the dominant kernel, from ncu captures
-# summarised under profiles/ (None where no capture exists for the workload).
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum);
+# absent where no capture exists for the workload.
 NCU_TRAFFIC_BYTES = {
-    "q4_0_11008x4096": 25_426_432,  # profiles/gemv_imma_q4_0_11008x4096.md
-    "q8_0_4096x4096": 17_874_688,   # profiles/gemv_imma_q8_0_4096x4096.md
-    "q8_0_prefill_512x4096x14336": 70_580_992,  # profiles/gemm_tc_q8_0_prefill_512x4096x14336.md
+    "q4_0_11008x4096": 25_444_352,
+    "q8_0_prefill_512x4096x14336": 70_580_992,
 }
 
 
