@@ -78,6 +78,8 @@ struct ImmaArgs {
     uint32_t team;         // warps sharing a tile (a power of two dividing warps)
     uint32_t slots;
     uint32_t unit_bytes;   // 16 * box_bytes
+    uint64_t ldx;          // floats between token vectors of x
+    uint64_t ldy;          // floats between token vectors of y
     DeviceStatus* status;
     // Fused all-gather (npeers > 0): each finished y row is also stored at
     // peer_y[k][peer_row_offset + row] on every peer (NVLink peer stores), and
@@ -221,67 +223,72 @@ __device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, boo
     }
 }
 
-// All consumer threads: build the table of blocks [0, nblocks) of x, 8
-// threads per block, every x load issued before any is used.
+// All consumer threads: build the tables of blocks [0, nblocks) of `ntok`
+// token vectors (x + k * ldx, table + k * tstride), 8 threads per block, all
+// (token, block) pairs in one pass with every x load issued before any is used.
 constexpr uint32_t kLimbPasses = 8;  // up to 8 * nthreads / 8 blocks staged in registers at once
 template <bool SUMS>
-__device__ __forceinline__ void build_pair_table(const float* __restrict__ x, uint32_t nblocks, uint32_t tid,
-                                                 uint32_t nthreads, uint8_t* table) {
+__device__ __forceinline__ void build_pair_table(const float* __restrict__ x, uint64_t ldx, uint32_t ntok,
+                                                 uint32_t nblocks, uint32_t tid, uint32_t nthreads, uint8_t* table,
+                                                 size_t tstride) {
     const uint32_t per_pass = nthreads / 8u;
     const uint32_t q = tid & 7u;
-    for (uint32_t base = 0; base < nblocks; base += per_pass * kLimbPasses) {
+    const uint32_t total = ntok * nblocks;
+    for (uint32_t base = 0; base < total; base += per_pass * kLimbPasses) {
         float4 v[kLimbPasses];
 #pragma unroll
         for (uint32_t k = 0; k < kLimbPasses; ++k) {
-            const uint32_t b = base + k * per_pass + tid / 8u;
-            v[k] = b < nblocks ? __ldg(reinterpret_cast<const float4*>(x + 32u * b + 4u * q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const uint32_t f = base + k * per_pass + tid / 8u;
+            const uint32_t tok = f / nblocks, b = f - tok * nblocks;
+            v[k] = f < total ? __ldg(reinterpret_cast<const float4*>(x + tok * ldx + 32u * b + 4u * q))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (uint32_t k = 0; k < kLimbPasses; ++k) {
-            const uint32_t b = base + k * per_pass + tid / 8u;
-            if (base + k * per_pass < nblocks) limb_block<SUMS>(v[k], b, q, b < nblocks, table);
+            const uint32_t f = base + k * per_pass + tid / 8u;
+            const uint32_t tok = f / nblocks, b = f - tok * nblocks;
+            // the 8 threads of a block share f, so they agree on `in` (the shuffles
+            // inside span exactly those 8 lanes)
+            if (base + k * per_pass < total) limb_block<SUMS>(v[k], b, q, f < total, table + tok * tstride);
         }
     }
 }
 
-// One segment of one tile: `valid` block pairs starting at r0p / r1p (tile
-// rows g and g+8 of the slot), their x side at pt (the pair table entries).
-// acc0 / acc1 collect rows g and g+8 (this lane's D columns).
-template <uint32_t TYPE, uint32_t SEG, bool GUARD>
-__device__ __forceinline__ void segment_dot(const uint8_t* r0p, const uint8_t* r1p, const uint8_t* pt, uint32_t valid,
-                                            uint32_t lane, uint32_t even_mask, float& acc0, float& acc1) {
+// One segment of one tile for NT token vectors: `valid` block pairs starting at
+// r0p / r1p (tile rows g and g+8 of the slot); token t's x side at
+// pt + t * tstride (its pair table entries).  The weight fragments are loaded
+// once and used for every token.  acc0[t] / acc1[t] collect rows g and g+8
+// (this lane's D columns).
+template <uint32_t TYPE, uint32_t SEG, bool GUARD, uint32_t NT>
+__device__ __forceinline__ void segment_dot(const uint8_t* r0p, const uint8_t* r1p, const uint8_t* pt, size_t tstride,
+                                            uint32_t valid, uint32_t lane, uint32_t even_mask, float (&acc0)[NT],
+                                            float (&acc1)[NT]) {
     constexpr uint32_t pb = Pair<TYPE>::kBytes;
     const uint32_t t = lane & 3u;
     const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;  // this lane's D block within a pair
-#pragma unroll
+    // one token: every pair unrolled; several: two pairs at a time (the token loop
+    // is unrolled, and its accumulators must stay in registers)
+    constexpr uint32_t kUnroll = NT == 1 ? SEG : 2u;
+#pragma unroll kUnroll
     for (uint32_t p = 0; p < SEG; ++p) {
         if (GUARD && p >= valid) break;
         const uint8_t* p0 = r0p + p * pb;
         const uint8_t* p1 = r1p + p * pb;
-        const uint2 w = *reinterpret_cast<const uint2*>(pt + p * kPairTableBytes + lane * 8u);
-        const int4 te = *reinterpret_cast<const int4*>(pt + p * kPairTableBytes + 256u + t * 16u);
-        // B registers: column g of the block-diagonal B is in the even block (k < 16) for g < 4
-        const uint32_t b0lo = w.x & even_mask, b1lo = w.x & ~even_mask;
-        const uint32_t b0hi = w.y & even_mask, b1hi = w.y & ~even_mask;
-        int d[4];
+        // A fragments: Q8_0 two IMMAs (h = 0, 1), Q4_0 the low and high nibbles
+        uint32_t A[2][4];
         if constexpr (TYPE == kQ8_0) {
-            d[0] = d[1] = d[2] = d[3] = 0;
 #pragma unroll
             for (uint32_t h = 0; h < 2; ++h) {
                 // even block: quant bytes 16h+4t.. at pair offset 2+16h+4t (2 mod 4)
                 const uint32_t o = 16u * h + 4u * t;
                 const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + o);
                 const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + o);
-                const uint32_t a0 = __funnelshift_r(e0[0], e0[1], 16);
-                const uint32_t a2 = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
-                const uint32_t a1 = __funnelshift_r(e1[0], e1[1], 16);
-                const uint32_t a3 = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
-                imma<false>(d, a0, a1, a2, a3, h ? b0hi : b0lo, h ? b1hi : b1lo);
+                A[h][0] = __funnelshift_r(e0[0], e0[1], 16);
+                A[h][1] = __funnelshift_r(e1[0], e1[1], 16);
+                A[h][2] = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
+                A[h][3] = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
             }
         } else {
-            // accumulators start at -8 * sum L of their column (the nibble offset)
-            d[0] = d[2] = te.y;
-            d[1] = d[3] = te.z;
             // even block quant bytes 4t.. at pair offset 2+4t; odd block at 20+4t
             const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + 4u * t);
             const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + 4u * t);
@@ -290,33 +297,62 @@ __device__ __forceinline__ void segment_dot(const uint8_t* r0p, const uint8_t* r
             const uint32_t w1 = __funnelshift_r(e1[0], e1[1], 16);
             const uint32_t w3 = *reinterpret_cast<const uint32_t*>(p1 + 20u + 4u * t);
             const uint32_t m = 0x0F0F0F0Fu;
-            imma<true>(d, w0 & m, w1 & m, w2 & m, w3 & m, b0lo, b1lo);
-            imma<true>(d, (w0 >> 4) & m, (w1 >> 4) & m, (w2 >> 4) & m, (w3 >> 4) & m, b0hi, b1hi);
+            A[0][0] = w0 & m;
+            A[0][1] = w1 & m;
+            A[0][2] = w2 & m;
+            A[0][3] = w3 & m;
+            A[1][0] = (w0 >> 4) & m;
+            A[1][1] = (w1 >> 4) & m;
+            A[1][2] = (w2 >> 4) & m;
+            A[1][3] = (w3 >> 4) & m;
         }
-        // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
-        const float xs = __int_as_float(te.x);
-        const int v0 = d[0] * 128 + d[1];
-        const int v1 = d[2] * 128 + d[3];
-        const float s0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk)) * xs;
-        const float s1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk)) * xs;
-        acc0 = fmaf(static_cast<float>(v0), s0, acc0);
-        acc1 = fmaf(static_cast<float>(v1), s1, acc1);
+        const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk));
+        const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk));
+#pragma unroll
+        for (uint32_t k = 0; k < NT; ++k) {
+            const uint8_t* ptk = pt + k * tstride + p * kPairTableBytes;
+            const uint2 w = *reinterpret_cast<const uint2*>(ptk + lane * 8u);
+            const int4 te = *reinterpret_cast<const int4*>(ptk + 256u + t * 16u);
+            // B registers: column g of the block-diagonal B is in the even block (k < 16) for g < 4
+            const uint32_t b0lo = w.x & even_mask, b1lo = w.x & ~even_mask;
+            const uint32_t b0hi = w.y & even_mask, b1hi = w.y & ~even_mask;
+            int d[4];
+            if constexpr (TYPE == kQ8_0) {
+                d[0] = d[1] = d[2] = d[3] = 0;
+                imma<false>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo);
+                imma<false>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
+            } else {
+                // accumulators start at -8 * sum L of their column (the nibble offset)
+                d[0] = d[2] = te.y;
+                d[1] = d[3] = te.z;
+                imma<true>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo);
+                imma<true>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
+            }
+            // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
+            const float xs = __int_as_float(te.x);
+            const int v0 = d[0] * 128 + d[1];
+            const int v1 = d[2] * 128 + d[3];
+            acc0[k] = fmaf(static_cast<float>(v0), d0 * xs, acc0[k]);
+            acc1[k] = fmaf(static_cast<float>(v1), d1 * xs, acc1[k]);
+        }
     }
 }
 
 // MULTI: the rows are cut into more than one column group.  SEG: block pairs
-// per unit.
-template <uint32_t TYPE, uint32_t SEG, bool MULTI>
-// At most 96 registers: registers are charged per group of four warps, so a
-// CTA of 17 warps is charged as 20 (20 x 32 x 96 = 61440 of 65536).
-__global__ void __maxnreg__(96)
+// per unit.  NT: token vectors per launch (x [NT][ldx], y [NT][ldy]).
+template <uint32_t TYPE, uint32_t SEG, bool MULTI, uint32_t NT>
+// Registers are charged per group of four warps: one token runs 16 consumer
+// warps (17 warps, charged as 20) within 96 registers; several tokens run at
+// most 8 (9 warps, charged as 12) within 128, room for the per-token accumulators.
+__global__ void __maxnreg__(NT == 1 ? 96 : 128)
     gemv_imma_kernel(const __grid_constant__ CUtensorMap map, const ImmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t S = a.slots, W = a.warps;
-    // [ring: S units][pair table][full S][empty S][team 8][issued S][team partial sums 2 x W x 16][abort flag]
+    // [ring: S units][pair table x NT][full S][empty S][team 8][issued S][partial sums 2 x W x NT x 16][abort flag]
     uint8_t* table = smem + static_cast<size_t>(S) * a.unit_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(table + static_cast<size_t>(a.group_pairs) * kPairTableBytes);
+    const size_t tstride = static_cast<size_t>(a.group_pairs) * kPairTableBytes;  // one token's table
+    uint64_t* full = reinterpret_cast<uint64_t*>(table + NT * tstride);
     uint64_t* empty = full + S;
     // issued[s]: the unit whose copy into slot s was last started.  A warp skips
     // the units of other warps, so it may reach a slot two or more uses ahead of
@@ -326,7 +362,7 @@ __global__ void __maxnreg__(96)
     uint64_t* teambar = empty + S;  // [8]: a team's partial sums are complete (K arrivals)
     volatile uint32_t* issued = reinterpret_cast<volatile uint32_t*>(teambar + 8);
     float* red = reinterpret_cast<float*>(const_cast<uint32_t*>(issued) + S);
-    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(red + 2u * W * 16u);
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(red + 2u * W * NT * 16u);
 
     // this CTA's tiles: an even split of all 16-row tiles
     const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * blockIdx.x / gridDim.x);
@@ -416,13 +452,16 @@ __global__ void __maxnreg__(96)
         const uint32_t gp = a.pairs_total - pair_g < a.group_pairs ? a.pairs_total - pair_g : a.group_pairs;
         const uint32_t nseg = (gp + SEG - 1u) / SEG;
         if (gi > 0) named_barrier_sync(1, W * 32u);  // every warp is done with the last group's table
-        build_pair_table<kQ4>(a.x + static_cast<size_t>(pair_g) * 64u, 2u * gp, threadIdx.x, W * 32u, table);
+        build_pair_table<kQ4>(a.x + static_cast<size_t>(pair_g) * 64u, a.ldx, NT, 2u * gp, threadIdx.x, W * 32u, table,
+                              tstride);
         named_barrier_sync(1, W * 32u);
         for (uint32_t tb = 0; tb < my_tiles; tb += teams) {
             const uint32_t j = tb + team;
             if (j >= my_tiles) break;  // the last block has fewer tiles than teams
             const uint32_t nb = my_tiles - tb < teams ? my_tiles - tb : teams;
-            float acc0 = 0.f, acc1 = 0.f;
+            float acc0[NT], acc1[NT];
+#pragma unroll
+            for (uint32_t k = 0; k < NT; ++k) acc0[k] = acc1[k] = 0.f;
             for (uint32_t s = member; s < nseg; s += K) {
                 const uint32_t uj = u + tb * nseg + s * nb + team;
                 const uint32_t slot = uj % S, parity = (uj / S) & 1u;
@@ -437,28 +476,38 @@ __global__ void __maxnreg__(96)
                     const uint32_t left = gp - s * SEG;
                     const uint8_t* pt = table + static_cast<size_t>(s) * SEG * kPairTableBytes;
                     if (left >= SEG)
-                        segment_dot<TYPE, SEG, false>(unit + off_a, unit + off_b, pt, SEG, lane, even_mask, acc0, acc1);
+                        segment_dot<TYPE, SEG, false, NT>(unit + off_a, unit + off_b, pt, tstride, SEG, lane, even_mask,
+                                                          acc0, acc1);
                     else
-                        segment_dot<TYPE, SEG, true>(unit + off_a, unit + off_b, pt, left, lane, even_mask, acc0, acc1);
+                        segment_dot<TYPE, SEG, true, NT>(unit + off_a, unit + off_b, pt, tstride, left, lane, even_mask,
+                                                         acc0, acc1);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[slot]);
                 }
             }
-            // fold the four t-lanes (columns) of each row
-            acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
-            acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
-            acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
-            acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
-            // row r of the tile: acc0 (r < 8) or acc1 (r >= 8) of lane 4 (r mod 8); lane r takes it
+            // per token: fold the four t-lanes (columns) of each row; row r of the tile is
+            // acc0 (r < 8) or acc1 (r >= 8) of lane 4 (r mod 8), and lane r takes it
             const uint32_t r = lane & 15u;
-            const float v0 = __shfl_sync(0xFFFFFFFFu, acc0, 4u * (r & 7u));
-            const float v1 = __shfl_sync(0xFFFFFFFFu, acc1, 4u * (r & 7u));
-            float v = r < 8 ? v0 : v1;
+            float v[NT];
+#pragma unroll
+            for (uint32_t k = 0; k < NT; ++k) {
+                float c0 = acc0[k], c1 = acc1[k];
+                c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
+                c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
+                c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
+                c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
+                const float v0 = __shfl_sync(0xFFFFFFFFu, c0, 4u * (r & 7u));
+                const float v1 = __shfl_sync(0xFFFFFFFFu, c1, 4u * (r & 7u));
+                v[k] = r < 8 ? v0 : v1;
+            }
             if (K > 1) {
                 // the team's partial sums meet in shared memory (two buffers by tile parity);
                 // member 0 adds them up in member order
-                float* rb = red + (static_cast<size_t>(2u * team + (round & 1u)) * K) * 16u;
-                if (lane < 16) rb[member * 16u + lane] = v;
+                float* rb = red + (static_cast<size_t>(2u * team + (round & 1u)) * K) * NT * 16u;
+                if (lane < 16) {
+#pragma unroll
+                    for (uint32_t k = 0; k < NT; ++k) rb[(member * NT + k) * 16u + lane] = v[k];
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&teambar[team]);
                 // every member waits (no member can arrive for the next round before this
@@ -468,17 +517,26 @@ __global__ void __maxnreg__(96)
                     *abort_flag = 1u;
                 }
                 if (member == 0) {
-                    v = rb[lane & 15u];
-                    for (uint32_t k = 1; k < K; ++k) v += rb[k * 16u + (lane & 15u)];
+#pragma unroll
+                    for (uint32_t k = 0; k < NT; ++k) {
+                        float sum = rb[k * 16u + r];
+                        for (uint32_t mm = 1; mm < K; ++mm) sum += rb[(mm * NT + k) * 16u + r];
+                        v[k] = sum;
+                    }
                 }
             }
             if (ok && member == 0 && lane < 16) {
                 const uint64_t row = static_cast<uint64_t>(tile_begin + j) * kTileRows + lane;
                 if (row < a.rows) {
-                    if (MULTI && gi > 0) v += a.y[row];  // groups add up in group order
-                    a.y[row] = v;
-                    if (a.npeers != 0u && gi + 1u == ngroups)
-                        for (uint32_t k = 0; k < a.npeers; ++k) a.peer_y[k][a.peer_row_offset + row] = v;
+#pragma unroll
+                    for (uint32_t k = 0; k < NT; ++k) {
+                        float* yr = a.y + k * a.ldy + row;
+                        float val = v[k];
+                        if (MULTI && gi > 0) val += *yr;  // groups add up in group order
+                        *yr = val;
+                        if (NT == 1 && a.npeers != 0u && gi + 1u == ngroups)
+                            for (uint32_t q = 0; q < a.npeers; ++q) a.peer_y[q][a.peer_row_offset + row] = val;
+                    }
                 }
             }
             ++round;
@@ -496,14 +554,14 @@ __global__ void __maxnreg__(96)
     }
 }
 
-template <uint32_t TYPE, uint32_t SEG, bool MULTI>
+template <uint32_t TYPE, uint32_t SEG, bool MULTI, uint32_t NT>
 cudaError_t launch_imma_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
                           bool pdl) {
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        auto k = gemv_imma_kernel<TYPE, SEG, MULTI>;
+        auto k = gemv_imma_kernel<TYPE, SEG, MULTI, NT>;
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         // the whole unified L1 as shared memory, so two 113 KB CTAs fit on an SM
         if (e == cudaSuccess)
@@ -521,20 +579,31 @@ cudaError_t launch_imma_t(const ImmaPlan& plan, const CUtensorMap& map, const Im
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, SEG, MULTI>, map, args);
+    return cudaLaunchKernelEx(&cfg, gemv_imma_kernel<TYPE, SEG, MULTI, NT>, map, args);
+}
+
+// One token: both group layouts; several tokens: the group-capable kernel only
+// (it also serves a single group).
+template <uint32_t TYPE, uint32_t SEG>
+cudaError_t launch_imma_s(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                          bool pdl) {
+    switch (plan.tokens) {
+        case 1: return plan.groups > 1 ? launch_imma_t<TYPE, SEG, true, 1>(plan, map, args, stream, pdl)
+                                       : launch_imma_t<TYPE, SEG, false, 1>(plan, map, args, stream, pdl);
+        case 2: return launch_imma_t<TYPE, SEG, true, 2>(plan, map, args, stream, pdl);
+        case 4: return launch_imma_t<TYPE, SEG, true, 4>(plan, map, args, stream, pdl);
+        case 8: return launch_imma_t<TYPE, SEG, true, 8>(plan, map, args, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <uint32_t TYPE>
 cudaError_t launch_imma_p(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
                           bool pdl) {
-    const bool multi = plan.groups > 1;
     switch (plan.seg_pairs) {
-        case 4: return multi ? launch_imma_t<TYPE, 4, true>(plan, map, args, stream, pdl)
-                             : launch_imma_t<TYPE, 4, false>(plan, map, args, stream, pdl);
-        case 8: return multi ? launch_imma_t<TYPE, 8, true>(plan, map, args, stream, pdl)
-                             : launch_imma_t<TYPE, 8, false>(plan, map, args, stream, pdl);
-        case 16: return multi ? launch_imma_t<TYPE, 16, true>(plan, map, args, stream, pdl)
-                              : launch_imma_t<TYPE, 16, false>(plan, map, args, stream, pdl);
+        case 4: return launch_imma_s<TYPE, 4>(plan, map, args, stream, pdl);
+        case 8: return launch_imma_s<TYPE, 8>(plan, map, args, stream, pdl);
+        case 16: return launch_imma_s<TYPE, 16>(plan, map, args, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -552,9 +621,10 @@ uint64_t box_row_bytes(uint64_t bp, uint64_t pair_bytes) {
 }  // namespace
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
-                   const ImmaTuning* tune) {
+                   const ImmaTuning* tune, uint32_t tokens) {
     ImmaPlan p;
     if (type != kQ8_0 && type != kQ4_0) return p;
+    if (tokens != 1 && tokens != 2 && tokens != 4 && tokens != 8) return p;
     // tensor-map coordinates are int32: rows below 2^31
     if (cols % 64u || cols > 0xFFFFFFFFull || rows == 0 || rows >= 0x80000000ull || num_sms <= 0) return p;
     const uint64_t rb = row_bytes_of(type, cols);
@@ -563,8 +633,7 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     const uint64_t pairs_total = cols / 64u;
     const ImmaTuning t = tune ? *tune : ImmaTuning{};
     const uint64_t tiles = (rows + kTileRows - 1) / kTileRows;
-    // One CTA per SM per launch, sized so two fit on an SM (the next launch's
-    // CTA beside it) unless a deeper ring is asked for.
+    // One CTA per SM per launch with the whole shared memory (a smaller budget on request).
     const bool wide = t.wide != 0;
     uint64_t budget = wide ? static_cast<uint64_t>(max_smem_optin) : kNarrowSmem;
     if (t.smem_budget && t.smem_budget < budget) budget = t.smem_budget;
@@ -572,23 +641,35 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     const uint64_t per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1u;
     const uint64_t grid = tiles < per_sm * num_sms ? tiles : per_sm * num_sms;
     const uint64_t tiles_per_cta = (tiles + grid - 1) / grid;
+    // consumer warps: 16 for one token; 8 for several (each unit's MMA work grows with
+    // the tokens, and 4 warps already keep the SM's int8 MMA pipe busy)
+    const uint64_t max_warps = tokens == 1 ? kMaxWarps : 8u;
     // unit: 16 rows x 16 block pairs (Q4_0, 9.5 KB) or 8 (Q8_0, 9 KB), halved
     // (down to 4) while a CTA would have fewer units than warps
     uint64_t seg = t.seg_pairs ? t.seg_pairs : (type == kQ4_0 ? 16u : 8u);
     if (seg != 4u && seg != 8u && seg != 16u) return p;
-    while (!t.seg_pairs && seg > 4u && (seg > pairs_total || tiles_per_cta * ((pairs_total + seg - 1) / seg) < kMaxWarps))
+    while (!t.seg_pairs && seg > 4u && (seg > pairs_total || tiles_per_cta * ((pairs_total + seg - 1) / seg) < max_warps))
         seg /= 2u;
-    const uint64_t box_bytes = box_row_bytes(seg, pair_bytes);
+    uint64_t box_bytes = box_row_bytes(seg, pair_bytes);
     if (box_bytes > kMaxBoxBytes) return p;
-    const uint64_t unit_bytes = kTileRows * box_bytes;  // a multiple of 256
-    // column group: the whole row when its table fits the table budget, else a
-    // multiple of the segment
-    const uint64_t table_budget = t.table_budget ? t.table_budget : 24u * 1024u;
+    uint64_t unit_bytes = kTileRows * box_bytes;  // a multiple of 256
+    // column group: the whole row when its tables (one per token) fit the table
+    // budget (24 KB for one token, 96 KB for several: their MMA work, not the ring,
+    // bounds them), else a multiple of the segment
+    uint64_t table_budget = t.table_budget ? t.table_budget : (tokens > 1 ? 96u : 24u) * 1024u;
+    if (!t.table_budget && budget > 4u * unit_bytes + 8192u && table_budget > budget - 4u * unit_bytes - 8192u)
+        table_budget = budget - 4u * unit_bytes - 8192u;  // leave room for a ring of 4 units
+    const uint64_t pair_table = kPairTableBytes * tokens;
     uint64_t group = align_up64(pairs_total, seg);
-    if (group * kPairTableBytes > table_budget) {
-        group = (table_budget / kPairTableBytes) / seg * seg;
+    if (group * pair_table > table_budget) {
+        group = (table_budget / pair_table) / seg * seg;
         if (group == 0) group = seg;
     }
+    // several tokens: narrower units while a CTA's share of a group has fewer
+    // units than warps (the MMA work, not the copies, bounds these)
+    while (tokens > 1 && !t.seg_pairs && seg > 4u && tiles_per_cta * ((group + seg - 1) / seg) < max_warps) seg /= 2u;
+    box_bytes = box_row_bytes(seg, pair_bytes);
+    unit_bytes = kTileRows * box_bytes;
     const uint64_t groups = (pairs_total + group - 1) / group;
     // Teams: a CTA with fewer tiles than warps lets 2, 4 or 8 warps share a tile
     // (each a share of its segments) so that up to 8 warps stay busy.
@@ -596,11 +677,11 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     // Team size K: the smallest power of two (at most the segments per tile)
     // that gives every warp a share, tiles x K >= warps.
     uint64_t team = 1;
-    while (team * 2u <= nseg && team * 2u <= kMaxWarps && tiles_per_cta * team < kMaxWarps) team *= 2u;
-    const uint64_t nteams = tiles_per_cta < kMaxWarps / team ? tiles_per_cta : kMaxWarps / team;
+    while (team * 2u <= nseg && team * 2u <= max_warps && tiles_per_cta * team < max_warps) team *= 2u;
+    const uint64_t nteams = tiles_per_cta < max_warps / team ? tiles_per_cta : max_warps / team;
     const uint64_t warps = nteams * team;
-    // table, 8 team barriers, partial sums, abort flag
-    const uint64_t fixed = group * kPairTableBytes + 64u + 2u * warps * 16u * 4u + 16u;
+    // tables, 8 team barriers, partial sums, abort flag
+    const uint64_t fixed = group * pair_table + 64u + 2u * warps * tokens * 16u * 4u + 16u;
     auto smem_of = [&](uint64_t s) { return s * unit_bytes + fixed + 20u * s; };
     // ring: the CTA's whole work when it fits, else the most slots that fit
     const uint64_t work = tiles_per_cta * groups * nseg;
@@ -613,6 +694,7 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     p.wide = wide;
     p.warps = static_cast<uint32_t>(warps);
     p.team = static_cast<uint32_t>(team);
+    p.tokens = tokens;
     p.seg_pairs = static_cast<uint32_t>(seg);
     p.tile_rows = kTileRows;
     p.tiles = static_cast<uint32_t>(tiles);
@@ -628,9 +710,15 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
 }
 
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
-                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather) {
+                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather, uint64_t ldx,
+                        uint64_t ldy) {
     if (!plan.ok || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
         return cudaErrorInvalidValue;
+    if (ldx == 0) ldx = cols;
+    if (ldy == 0) ldy = rows;
+    // x rows are read as float4: every token vector starts on a 16-byte boundary
+    if (plan.tokens > 1 && (ldx % 4u != 0 || ldx < cols || ldy < rows)) return cudaErrorInvalidValue;
+    if (gather != nullptr && plan.tokens != 1) return cudaErrorInvalidValue;
     ImmaArgs a{};
     if (gather != nullptr) {
         if (gather->npeers > kMaxPeers) return cudaErrorInvalidValue;
@@ -664,6 +752,8 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
     a.team = plan.team;
     a.slots = plan.slots;
     a.unit_bytes = plan.unit_bytes;
+    a.ldx = ldx;
+    a.ldy = ldy;
     a.status = status;
     if (plan.type == kQ8_0) return launch_imma_p<kQ8_0>(plan, map, a, stream, pdl);
     return launch_imma_p<kQ4_0>(plan, map, a, stream, pdl);

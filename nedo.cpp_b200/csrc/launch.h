@@ -63,6 +63,7 @@ struct ImmaPlan {
     uint32_t type = 0;
     uint32_t warps = 0;        // consumer warps; one more warp streams units
     uint32_t team = 0;         // warps sharing one tile (its segments split among them)
+    uint32_t tokens = 0;       // token vectors per launch (1, 2, 4 or 8)
     uint32_t seg_pairs = 0;    // block pairs per unit
     uint32_t tile_rows = 0;    // 16
     uint32_t tiles = 0;        // ceil(rows / 16)
@@ -85,7 +86,7 @@ struct ImmaTuning {
 };
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
-                   const ImmaTuning* tune = nullptr);
+                   const ImmaTuning* tune = nullptr, uint32_t tokens = 1);
 
 // Fused all-gather of a row-sharded matvec over NVLink: the kernel also stores
 // its rows into every peer's gathered y and counts each finished CTA on the
@@ -97,8 +98,11 @@ struct PeerGather {
     float* peer_y[kMaxPeers] = {};     // each peer's gathered y (peer device pointers)
     uint32_t* peer_signal[kMaxPeers] = {};
 };
+// plan.tokens token vectors: x [tokens][ldx], y [tokens][ldy] (0 = cols / rows);
+// every weight unit is read once for all of them.
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
-                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr);
+                        DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr,
+                        uint64_t ldx = 0, uint64_t ldy = 0);
 
 // One thread waits (bounded, 2 s) until *signal has advanced by `increment`
 // past *expected, then advances *expected: the peers' rows are visible after it.

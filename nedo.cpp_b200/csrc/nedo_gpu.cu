@@ -228,14 +228,23 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
         return 0;
     }
     if (batch > 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
-        // small batches of quantised rows: the int8 tensor-pipe matvec per vector
-        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
-        if (ip.ok) {
-            for (uint32_t b = 0; b < batch; ++b) {
-                cudaError_t e = launch_imma(ip, w, x + static_cast<uint64_t>(b) * cols,
+        // small batches of quantised rows: the int8 tensor-pipe kernel with up to 8
+        // token vectors per launch (each weight unit read once for all of them)
+        ImmaPlan plans[4];
+        bool ok = true;
+        for (uint32_t i = 0; i < 4 && ok; ++i) {
+            plans[i] = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, 1u << i);
+            ok = plans[i].ok;
+        }
+        if (ok) {
+            for (uint32_t b = 0; b < batch;) {
+                uint32_t i = 3;
+                while ((1u << i) > batch - b) --i;
+                cudaError_t e = launch_imma(plans[i], w, x + static_cast<uint64_t>(b) * cols,
                                             y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, stream,
-                                            g_pdl.load() != 0);
+                                            g_pdl.load() != 0, nullptr, cols, rows);
                 if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch");
+                b += 1u << i;
             }
             return 0;
         }
@@ -545,8 +554,9 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
     const bool tc = batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch);
-    if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // one int8 tensor-pipe launch per vector
-        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+    if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
+        const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;
+        ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, tokens);
         if (ip.ok) {
             out[0] = 4;
             out[1] = ip.grid;

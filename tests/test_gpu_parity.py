@@ -126,6 +126,24 @@ def test_batched_matches_serial_reference(lib, cuda, oracle, t):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"batch item {b}")
 
 
+# Batches of 2-15 quantised vectors run the int8 tensor-pipe kernel with 8, 4, 2
+# and 1 token vectors per launch (every weight unit read once per launch): each
+# vector must match the reference's serial matvec.  Shapes cover a ragged last
+# tile, rows cut into several column groups (8192 columns) and short rows.
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0])
+@pytest.mark.parametrize("rows,cols,batch", [(333, 2048, 2), (333, 2048, 7), (100, 8192, 13), (4096, 1536, 15),
+                                             (1000, 4096, 4)])
+def test_small_batch_int8_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
+    plan = lib.plan_info(t, rows, cols, batch)
+    assert plan["path"] == 4, plan
+    w = B.gen_weight(t, rows, cols, 41 + batch)
+    x = B.gen_x(cols, 41 + batch, batch=batch)
+    y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    ref = oracle.matvec_batch(t, rows, cols, w, x)
+    for b in range(batch):
+        assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"batch item {b}")
+
+
 # Batches of >= 16 vectors run as one tcgen05 GEMM (fp16 x and d*q, fp32
 # accumulation): the same per-element tolerance against the reference's serial
 # matvecs.  Shapes cover ragged token tiles (tiles of 256), ragged row tiles
