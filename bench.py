@@ -94,6 +94,8 @@ def sweep_bytes(wl, batch):
 # absent where no capture exists for the workload.
 NCU_TRAFFIC_BYTES = {
     "q4_0_11008x4096": 25_444_352,
+    "q8_0_4096x4096": 17_893_632,
+    "q4_0_32768x32768": 609_625_344,
     "q8_0_prefill_512x4096x14336": 70_580_992,
 }
 
