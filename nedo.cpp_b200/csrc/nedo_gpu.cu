@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <atomic>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -42,10 +43,23 @@ int cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
     } while (0)
 
+// A resident weight, and the CUDA graph of the host entry point's call on it
+// (x upload, matvec, y and status download) once the call has run eagerly.
 struct Resident {
     void* dev = nullptr;
     uint64_t bytes = 0;
+    cudaGraphExec_t call = nullptr;
+    uint32_t type = 0;
+    uint64_t rows = 0, cols = 0;
+    const void* bufs[5] = {};  // staging buffers the graph was captured with
 };
+
+void release_resident(Resident& r) {
+    if (r.call) cudaGraphExecDestroy(r.call);
+    r.call = nullptr;
+    if (r.dev) cudaFree(r.dev);
+    r.dev = nullptr;
+}
 
 struct DeviceState {
     int device = -1;
@@ -166,7 +180,7 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
         return 0;
     }
     if (it != s->cache.end()) {
-        cudaFree(it->second.dev);
+        release_resident(it->second);
         s->cache.erase(it);
     }
     void* d = nullptr;
@@ -174,7 +188,7 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
     if (e == cudaErrorMemoryAllocation) {
         // Out of room: drop every other resident weight and retry once.
         cudaGetLastError();
-        for (auto& kv : s->cache) cudaFree(kv.second.dev);
+        for (auto& kv : s->cache) release_resident(kv.second);
         s->cache.clear();
         e = cudaMalloc(&d, w_bytes ? w_bytes : 16);
     }
@@ -186,7 +200,10 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
             return cuda_fail(e, "cudaMemcpy(weight upload)");
         }
     }
-    s->cache[w_host] = Resident{d, w_bytes};
+    Resident r;
+    r.dev = d;
+    r.bytes = w_bytes;
+    s->cache[w_host] = r;
     *w_dev = d;
     return 0;
 }
@@ -198,12 +215,13 @@ constexpr uint32_t kTensorCoreMinBatch = 16;
 
 // The one dispatch point for every matvec launch.
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
-                    float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream) {
+                    float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream, int pdl_override = -1) {
     if (rows == 0 || batch == 0) return 0;
+    const bool use_pdl = pdl_override < 0 ? g_pdl.load() != 0 : pdl_override != 0;
     if (batch == 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
         if (ip.ok) {
-            cudaError_t e = launch_imma(ip, w, x, y, rows, cols, s->status, stream, g_pdl.load() != 0);
+            cudaError_t e = launch_imma(ip, w, x, y, rows, cols, s->status, stream, use_pdl);
             if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch");
             return 0;
         }
@@ -211,7 +229,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
     if (batch == 1 && aligned16(w) && aligned16(x)) {
         StreamPlan plan = plan_stream(type, rows, cols, s->num_sms, s->max_smem);
         if (plan.ok) {
-            cudaError_t e = launch_stream(type, plan, w, x, y, rows, cols, s->status, amax, stream, g_pdl.load() != 0);
+            cudaError_t e = launch_stream(type, plan, w, x, y, rows, cols, s->status, amax, stream, use_pdl);
             if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
             return 0;
         }
@@ -242,7 +260,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
                 while ((1u << i) > batch - b) --i;
                 cudaError_t e = launch_imma(plans[i], w, x + static_cast<uint64_t>(b) * cols,
                                             y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, stream,
-                                            g_pdl.load() != 0, nullptr, cols, rows);
+                                            use_pdl, nullptr, cols, rows);
                 if (e != cudaSuccess) return cuda_fail(e, "gemv_imma launch");
                 b += 1u << i;
             }
@@ -255,7 +273,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             for (uint32_t b = 0; b < batch; ++b) {
                 cudaError_t e = launch_stream(type, plan, w, x + static_cast<uint64_t>(b) * cols,
                                               y + static_cast<uint64_t>(b) * rows, rows, cols, s->status, nullptr,
-                                              stream, g_pdl.load() != 0);
+                                              stream, use_pdl);
                 if (e != cudaSuccess) return cuda_fail(e, "gemv_stream launch");
             }
             return 0;
@@ -354,10 +372,56 @@ int nedo_gpu_matvec(uint32_t type, uint64_t rows, uint64_t cols, const void* w_h
     if (int rc = ensure_pin(&s->x_pin, &s->xp_cap, cols)) return rc;
     if (int rc = ensure_pin(&s->y_pin, &s->yp_cap, rows)) return rc;
     std::memcpy(s->x_pin, x_host, cols * sizeof(float));
-    NEDO_CUDA_TRY(cudaMemcpyAsync(s->x_dev, s->x_pin, cols * sizeof(float), cudaMemcpyHostToDevice, s->stream));
-    if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, 1, nullptr, s->stream)) return rc;
-    NEDO_CUDA_TRY(cudaMemcpyAsync(s->y_pin, s->y_dev, rows * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
-    if (int rc = read_status(s, s->stream)) return rc;
+    // The call as one sequence on the library's stream: x up, matvec, y and the
+    // status word down.  The first call on a weight runs it eagerly; later calls
+    // replay a CUDA graph of it (one launch instead of four).
+    Resident& r = s->cache[w_host];
+    const void* bufs[5] = {s->x_dev, s->y_dev, s->x_pin, s->y_pin, s->status_pin};
+    auto enqueue = [&]() -> int {
+        NEDO_CUDA_TRY(cudaMemcpyAsync(s->x_dev, s->x_pin, cols * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+        if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, 1, nullptr, s->stream, 0))
+            return rc;
+        NEDO_CUDA_TRY(cudaMemcpyAsync(s->y_pin, s->y_dev, rows * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+        NEDO_CUDA_TRY(
+            cudaMemcpyAsync(s->status_pin, s->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, s->stream));
+        return 0;
+    };
+    const bool replay = r.call != nullptr && r.type == type && r.rows == rows && r.cols == cols &&
+                        std::equal(bufs, bufs + 5, r.bufs);
+    if (replay) {
+        NEDO_CUDA_TRY(cudaGraphLaunch(r.call, s->stream));
+    } else {
+        if (r.call) cudaGraphExecDestroy(r.call);
+        r.call = nullptr;
+        if (int rc = enqueue()) return rc;
+        // capture the same sequence for the next calls (a failure only costs the replay)
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int rc = enqueue();
+            const cudaError_t ec = cudaStreamEndCapture(s->stream, &g);
+            if (rc == 0 && ec == cudaSuccess && g != nullptr &&
+                cudaGraphInstantiate(&r.call, g, 0) == cudaSuccess) {
+                r.type = type;
+                r.rows = rows;
+                r.cols = cols;
+                std::copy(bufs, bufs + 5, r.bufs);
+            } else {
+                r.call = nullptr;
+            }
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+        }
+    }
+    NEDO_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (s->status_pin->flags != 0) {
+        const DeviceStatus st = *s->status_pin;
+        cudaMemsetAsync(s->status, 0, sizeof(DeviceStatus), s->stream);
+        cudaStreamSynchronize(s->stream);
+        char buf[160];
+        std::snprintf(buf, sizeof(buf), "device kernel gave up on a bounded wait (flags=0x%x, site=%u)", st.flags,
+                      st.where);
+        return fail(NEDO_GPU_ERR_DEVICE, buf);
+    }
     std::memcpy(y_host, s->y_pin, rows * sizeof(float));
     return 0;
 }
@@ -399,7 +463,7 @@ int nedo_gpu_weight_evict(const void* w_host) {
     std::lock_guard<std::mutex> lk(s->mu);
     auto it = s->cache.find(w_host);
     if (it != s->cache.end()) {
-        cudaFree(it->second.dev);
+        release_resident(it->second);
         s->cache.erase(it);
     }
     return 0;
@@ -413,7 +477,7 @@ int nedo_gpu_cache_clear(void) {
         if (s == nullptr) continue;
         std::lock_guard<std::mutex> lk2(s->mu);
         cudaSetDevice(s->device);
-        for (auto& kv : s->cache) cudaFree(kv.second.dev);
+        for (auto& kv : s->cache) release_resident(kv.second);
         s->cache.clear();
     }
     cudaSetDevice(prev);

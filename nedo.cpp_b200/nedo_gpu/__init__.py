@@ -117,11 +117,14 @@ class Library:
     # ------------------------------------------------------- host entry points
     def matvec(self, type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
         """nedo::kernels::matvec: y[r] = dot(row r, x).  w holds the GGUF bytes."""
-        w = np.ascontiguousarray(w)
-        x = np.ascontiguousarray(x, dtype=np.float32)
+        if not (isinstance(w, np.ndarray) and w.flags.c_contiguous):
+            w = np.ascontiguousarray(w)
+        if not (isinstance(x, np.ndarray) and x.dtype == np.float32 and x.flags.c_contiguous):
+            x = np.ascontiguousarray(x, dtype=np.float32)
         y = np.empty(rows, dtype=np.float32)
-        self._check(self.lib.nedo_gpu_matvec(type_, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data,
-                                             y.ctypes.data))
+        # raw addresses from the array interface (cheaper than .ctypes per call)
+        self._check(self.lib.nedo_gpu_matvec(type_, rows, cols, w.__array_interface__["data"][0], w.nbytes,
+                                             x.__array_interface__["data"][0], y.__array_interface__["data"][0]))
         return y
 
     def embedding_row(self, type_: int, rows: int, cols: int, w: np.ndarray, row: int) -> np.ndarray:

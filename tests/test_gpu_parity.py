@@ -105,6 +105,29 @@ def test_generic_path_odd_blocks_and_unaligned(lib, cuda, oracle, t):
                       what="unaligned")
 
 
+# The host entry point replays a captured CUDA graph of its call from the second
+# call on a weight: repeated calls with new x, interleaved weights, and the same
+# weight bytes read as another shape must all match the oracle.
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
+def test_host_api_repeated_calls(lib, cuda, oracle, t):
+    rows, cols = 700, 2048
+    wa = B.gen_weight(t, rows, cols, 51)
+    wb = B.gen_weight(t, rows, cols, 52)
+    for i in range(4):
+        for w in (wa, wb):
+            x = B.gen_x(cols, 60 + i)
+            y = lib.matvec(t, rows, cols, w, x)
+            assert_within_tol(y, oracle.matvec(t, rows, cols, w, x), oracle.abs_dot(t, rows, cols, w, x),
+                              what=f"call {i}")
+    # the same bytes as twice the rows of half the columns
+    r2, c2 = 2 * rows, cols // 2
+    x = B.gen_x(c2, 70)
+    y = lib.matvec(t, r2, c2, wa, x)
+    assert_within_tol(y, oracle.matvec(t, r2, c2, wa, x), oracle.abs_dot(t, r2, c2, wa, x), what="reshaped")
+    lib.weight_evict(wa)
+    lib.weight_evict(wb)
+
+
 @pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
 def test_deterministic(lib, cuda, t):
     rows, cols = 3000, 4096
