@@ -231,6 +231,8 @@ struct Idx {
 
 // x (fp32, tokens x cols) -> fp16 (round to nearest), same layout.
 __global__ void x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ xh, uint64_t n) {
+    // the GEMM that reads xh may launch now: it streams its weights until this grid completes
+    asm volatile("griddepcontrol.launch_dependents;");
     for (uint64_t i = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) * 4u; i < n;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x * 4u) {
         if (i + 4u <= n) {
@@ -298,22 +300,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            grid_dependency_wait();  // X may come from the previous kernel
             uint32_t issued_ks = 0, issued_kc = 0;
             bool ok = true;
+            // raw weight chunk kc into its slot (the weights are not written by the
+            // previous kernel, so the first slots fill before its completion)
+            auto load_raw = [&](uint32_t kc) {
+                const uint32_t rs = kc % kRawSlots;
+                mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
+                // the chunk's first byte, rounded down to 16 bytes (uint16 elements)
+                const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
+                tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
+                            static_cast<int32_t>(row0), &raw_full[rs]);
+                issued_kc = kc + 1u;
+            };
+            if constexpr (kRawW)
+                for (uint32_t kc = 0; kc < kRawSlots && kc < chunks; ++kc) load_raw(kc);
+            grid_dependency_wait();  // X may come from the previous kernel
             for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
                 if constexpr (kRawW) {
                     const uint32_t rs = kc % kRawSlots;
-                    if (kc >= kRawSlots && !mbar_wait_bounded(&raw_empty[rs], ((kc / kRawSlots) - 1u) & 1u, a.status, 31u)) {
-                        ok = false;
-                        break;
+                    if (kc >= kRawSlots) {
+                        if (!mbar_wait_bounded(&raw_empty[rs], ((kc / kRawSlots) - 1u) & 1u, a.status, 31u)) {
+                            ok = false;
+                            break;
+                        }
+                        load_raw(kc);
                     }
-                    mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-                    // the chunk's first byte, rounded down to 16 bytes (uint16 elements)
-                    const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
-                    tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
-                                static_cast<int32_t>(row0), &raw_full[rs]);
-                    issued_kc = kc + 1u;
                 }
                 for (uint32_t j = 0; j < kRawK / kBK; ++j) {
                     const uint32_t ks = kc * (kRawK / kBK) + j;
@@ -478,9 +490,19 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     a.tokens = tokens;
     a.ldy = ldy;
     a.status = status;
-    const dim3 grid((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN);
-    gemm_tc_kernel<TYPE><<<grid, kThreads, smem, stream>>>(mw, mx, a);
-    return cudaGetLastError();
+    // programmatic dependent launch: the CTAs start (TMEM, barriers, the first
+    // weight chunks and their dequantisation) while the previous kernel finishes
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TYPE>, mw, mx, a);
 }
 
 }  // namespace
