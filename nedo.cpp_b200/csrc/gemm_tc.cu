@@ -80,11 +80,13 @@ constexpr uint32_t raw_row_bytes() {
 }
 
 struct GemmArgs {
-    float* y;          // [tokens][ldy]
-    uint32_t rows;     // N of the weight (output features)
-    uint32_t cols;     // K
+    float* y;              // [tokens][ldy]; split z writes y + z * split_stride
+    uint32_t rows;         // N of the weight (output features)
+    uint32_t cols;         // K
     uint32_t tokens;
     uint32_t ldy;
+    uint32_t ksplit;       // CTAs along K per tile (gridDim.z): each sums a range of raw chunks
+    uint64_t split_stride;
     DeviceStatus* status;
 };
 
@@ -273,6 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tok0 = blockIdx.y * kBN;   // tokens of this tile
     const uint32_t ksteps = (a.cols + kBK - 1) / kBK;
     const uint32_t chunks = (a.cols + kRawK - 1) / kRawK;
+    // this CTA's share of K: raw chunks [kc_begin, kc_end), k-steps [ks_begin, ks_end)
+    const uint32_t kc_begin = static_cast<uint32_t>(static_cast<uint64_t>(chunks) * blockIdx.z / a.ksplit);
+    const uint32_t kc_end = static_cast<uint32_t>(static_cast<uint64_t>(chunks) * (blockIdx.z + 1) / a.ksplit);
+    const uint32_t ks_begin = kc_begin * (kRawK / kBK);
+    const uint32_t ks_end = kc_end * (kRawK / kBK) < ksteps ? kc_end * (kRawK / kBK) : ksteps;
+    float* const y = a.y + blockIdx.z * a.split_stride;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kS; ++s) {
@@ -305,22 +313,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             // raw weight chunk kc into its slot (the weights are not written by the
             // previous kernel, so the first slots fill before its completion)
             auto load_raw = [&](uint32_t kc) {
-                const uint32_t rs = kc % kRawSlots;
+                const uint32_t rs = (kc - kc_begin) % kRawSlots;
                 mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
                 // the chunk's first byte, rounded down to 16 bytes (uint16 elements)
                 const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
                 tma_load_2d(sRaw + rs * kRawBytes, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
                             static_cast<int32_t>(row0), &raw_full[rs]);
-                issued_kc = kc + 1u;
+                issued_kc = kc - kc_begin + 1u;  // local count
             };
             if constexpr (kRawW)
-                for (uint32_t kc = 0; kc < kRawSlots && kc < chunks; ++kc) load_raw(kc);
+                for (uint32_t kc = kc_begin; kc < kc_begin + kRawSlots && kc < kc_end; ++kc) load_raw(kc);
             grid_dependency_wait();  // X may come from the previous kernel
-            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
+            for (uint32_t kc = kc_begin; kc < kc_end && ok; ++kc) {
                 if constexpr (kRawW) {
-                    const uint32_t rs = kc % kRawSlots;
-                    if (kc >= kRawSlots) {
-                        if (!mbar_wait_bounded(&raw_empty[rs], ((kc / kRawSlots) - 1u) & 1u, a.status, 31u)) {
+                    const uint32_t lc = kc - kc_begin;  // local chunk index: slot and phase
+                    const uint32_t rs = lc % kRawSlots;
+                    if (lc >= kRawSlots) {
+                        if (!mbar_wait_bounded(&raw_empty[rs], ((lc / kRawSlots) - 1u) & 1u, a.status, 31u)) {
                             ok = false;
                             break;
                         }
@@ -329,9 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 for (uint32_t j = 0; j < kRawK / kBK; ++j) {
                     const uint32_t ks = kc * (kRawK / kBK) + j;
-                    if (ks >= ksteps) break;
-                    const uint32_t s = ks % kS;
-                    if (ks >= kS && !mbar_wait_bounded(&ab_empty[s], ((ks / kS) - 1u) & 1u, a.status, 32u)) {
+                    if (ks >= ks_end) break;
+                    const uint32_t ls = ks - ks_begin;  // local k-step: stage and phase
+                    const uint32_t s = ls % kS;
+                    if (ls >= kS && !mbar_wait_bounded(&ab_empty[s], ((ls / kS) - 1u) & 1u, a.status, 32u)) {
                         ok = false;
                         break;
                     }
@@ -341,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if constexpr (!kRawW)
                         tma_load_2d(sA + s * kStageA, &map_w, static_cast<int32_t>(ks * kBK),
                                     static_cast<int32_t>(row0), &b_full[s]);
-                    issued_ks = ks + 1u;
+                    issued_ks = ls + 1u;
                 }
             }
             // drain: the last copies issued into every slot have landed before exit
@@ -354,8 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
-            for (uint32_t ks = 0; ks < ksteps && ok; ++ks) {
-                const uint32_t s = ks % kS, ph = (ks / kS) & 1u;
+            for (uint32_t ls = 0; ls < ks_end - ks_begin && ok; ++ls) {
+                const uint32_t s = ls % kS, ph = (ls / kS) & 1u;
                 ok = mbar_wait_bounded(&b_full[s], ph, a.status, 33u);
                 if constexpr (kRawW) ok = ok && mbar_wait_bounded(&a_full[s], ph, a.status, 34u);
                 if (!ok) break;
@@ -366,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t ad = sw64_desc(sA + s * kStageA + h * (kBM * 64u));
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // K = 16 per MMA: 32 bytes along the row
-                        tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, kIdesc, (ks | kk) != 0u);
+                        tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, kIdesc, (ls | kk) != 0u);
                 }
                 tc_commit(&ab_empty[s]);
             }
@@ -378,9 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t half = r / kBM;           // which MMA half-tile the row belongs to
         if constexpr (kRawW) {
             bool ok = true;
-            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
-                const uint32_t rs = kc % kRawSlots;
-                if (!mbar_wait_bounded(&raw_full[rs], (kc / kRawSlots) & 1u, a.status, 35u)) {
+            for (uint32_t kc = kc_begin; kc < kc_end && ok; ++kc) {
+                const uint32_t lc = kc - kc_begin;
+                const uint32_t rs = lc % kRawSlots;
+                if (!mbar_wait_bounded(&raw_full[rs], (lc / kRawSlots) & 1u, a.status, 35u)) {
                     ok = false;
                     break;
                 }
@@ -389,9 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 auto stage = [&](auto J) {
                     constexpr uint32_t j = decltype(J)::value;
                     const uint32_t ks = kc * (kRawK / kBK) + j;
-                    if (!ok || ks >= ksteps) return;
-                    const uint32_t s = ks % kS;
-                    if (ks >= kS && !mbar_wait_bounded(&ab_empty[s], ((ks / kS) - 1u) & 1u, a.status, 36u)) {
+                    if (!ok || ks >= ks_end) return;
+                    const uint32_t ls = ks - ks_begin;
+                    const uint32_t s = ls % kS;
+                    if (ls >= kS && !mbar_wait_bounded(&ab_empty[s], ((ls / kS) - 1u) & 1u, a.status, 36u)) {
                         ok = false;
                         return;
                     }
@@ -426,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (uint32_t i = 0; i < 32; ++i) {
                         const uint32_t t = tok0 + col + i;
-                        if (t < a.tokens) a.y[static_cast<size_t>(t) * a.ldy + wrow] = __uint_as_float(v[i]);
+                        if (t < a.tokens) y[static_cast<size_t>(t) * a.ldy + wrow] = __uint_as_float(v[i]);
                     }
                 }
             }
@@ -440,10 +452,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Split-K fold: y[t][r] = sum over z (in z order) of ws[z][t][r].  ws is written
+// by the GEMM launched just before, so the fold waits for that kernel first.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __restrict__ y, uint32_t splits,
+                                     uint32_t tokens, uint32_t rows, uint64_t ldy) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint64_t n = static_cast<uint64_t>(tokens) * rows;
+    const uint64_t zstride = n;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        float v = ws[i];
+        for (uint32_t z = 1; z < splits; ++z) v += ws[z * zstride + i];
+        const uint64_t t = i / rows, r = i - t * rows;
+        y[t * ldy + r] = v;
+    }
+}
+
 // ---- host side ----------------------------------------------------------
 template <uint32_t TYPE>
 cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
-                     uint32_t ldy, DeviceStatus* status, cudaStream_t stream) {
+                     uint32_t ldy, uint32_t ksplit, uint64_t split_stride, DeviceStatus* status, cudaStream_t stream) {
     EncodeTiled enc = encode_tiled_fn();
     if (enc == nullptr) return cudaErrorNotSupported;
     CUtensorMap mw, mx;
@@ -489,11 +517,13 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     a.cols = cols;
     a.tokens = tokens;
     a.ldy = ldy;
+    a.ksplit = ksplit;
+    a.split_stride = split_stride;
     a.status = status;
     // programmatic dependent launch: the CTAs start (TMEM, barriers, the first
     // weight chunks and their dequantisation) while the previous kernel finishes
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN);
+    cfg.gridDim = dim3((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN, ksplit);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -532,6 +562,35 @@ uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens) {
     return static_cast<uint32_t>(((rows + kRows - 1) / kRows) * ((tokens + kBN - 1) / kBN));
 }
 
+uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms) {
+    // tiles that leave most SMs idle share each tile's K among several CTAs
+    const uint64_t tiles = gemm_tc_ctas(rows, tokens);
+    const uint64_t chunks = (cols + kRawK - 1) / kRawK;
+    if (num_sms <= 0 || tiles * 2u >= static_cast<uint64_t>(num_sms)) return 1;
+    uint64_t s = static_cast<uint64_t>(num_sms) / tiles;
+    if (s > chunks) s = chunks;
+    return s < 1 ? 1u : static_cast<uint32_t>(s);
+}
+
+cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uint64_t tokens, uint64_t rows,
+                                 uint64_t ldy, int num_sms, cudaStream_t stream) {
+    const uint64_t n = tokens * rows;
+    uint64_t blocks = (n + 255u) / 256u;
+    if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
+    if (blocks == 0) blocks = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<uint32_t>(blocks));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, ws, y, splits, static_cast<uint32_t>(tokens),
+                              static_cast<uint32_t>(rows), ldy);
+}
+
 cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream) {
     uint64_t blocks = (n / 4u + 255u) / 256u;
     if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
@@ -541,13 +600,18 @@ cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms,
 }
 
 cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
-                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream) {
+                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream, uint32_t ksplit,
+                           uint64_t split_stride) {
     if (!gemm_tc_supported(type, rows, cols, tokens)) return cudaErrorInvalidValue;
+    if (ksplit == 0 || ksplit > (cols + kRawK - 1) / kRawK || ksplit > 65535u) return cudaErrorInvalidValue;
     const uint32_t r = static_cast<uint32_t>(rows), c = static_cast<uint32_t>(cols), t = static_cast<uint32_t>(tokens);
     switch (type) {
-        case kQ8_0: return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
-        case kQ4_0: return launch_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
-        case kF16: return launch_t<kF16>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        case kQ8_0:
+            return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
+        case kQ4_0:
+            return launch_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
+        case kF16:
+            return launch_t<kF16>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -77,6 +77,8 @@ struct DeviceState {
     DeviceStatus* status_pin = nullptr;
     __half* xh = nullptr;  // fp16 copy of the token vectors for the tensor-core GEMM
     uint64_t xh_cap = 0;
+    float* splitk_ws = nullptr;  // split-K partial sums of the tensor-core GEMM
+    uint64_t splitk_cap = 0;
     std::unordered_map<const void*, Resident> cache;
     std::mutex mu;
 };
@@ -210,8 +212,13 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Batches of at least this many token vectors run as one tensor-core GEMM.
+// Batches of at least this many token vectors run as one tensor-core GEMM, for
+// rows of at least kTensorCoreMinCols elements.  The GEMM rounds x and d*q to fp16
+// (worst case 2 * 2^-11 * sum|w*x| per output); its errors average out over the
+// row, and rows of 1024 elements and more keep them inside 1e-4 * sum|w*x| on
+// the test distributions.  Shorter rows use the exact int8 kernel.
 constexpr uint32_t kTensorCoreMinBatch = 16;
+constexpr uint64_t kTensorCoreMinCols = 1024;
 
 // The one dispatch point for every matvec launch.
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
@@ -234,13 +241,25 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             return 0;
         }
     }
-    if (batch >= kTensorCoreMinBatch && amax == nullptr && aligned16(w) && aligned16(x) &&
-        gemm_tc_supported(type, rows, cols, batch)) {
+    if (batch >= kTensorCoreMinBatch && cols >= kTensorCoreMinCols && amax == nullptr && aligned16(w) &&
+        aligned16(x) && gemm_tc_supported(type, rows, cols, batch)) {
         // tokens as the N dimension of a tcgen05 GEMM (x rounded to fp16 once)
         const uint64_t n = static_cast<uint64_t>(batch) * cols;
         if (int rc = ensure_dev(&s->xh, &s->xh_cap, n)) return rc;
         cudaError_t e = launch_x_to_f16(x, s->xh, n, s->num_sms, stream);
         if (e != cudaSuccess) return cuda_fail(e, "x to fp16 launch");
+        const uint32_t splits = gemm_tc_splits(rows, cols, batch, s->num_sms);
+        if (splits > 1) {
+            // few tiles: K shared among CTAs, partial sums folded in split order
+            if (int rc = ensure_dev(&s->splitk_ws, &s->splitk_cap, static_cast<uint64_t>(splits) * batch * rows))
+                return rc;
+            e = launch_gemm_tc(type, w, s->xh, s->splitk_ws, rows, cols, batch, rows, s->status, stream, splits,
+                               static_cast<uint64_t>(batch) * rows);
+            if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
+            e = launch_splitk_reduce(s->splitk_ws, y, splits, batch, rows, rows, s->num_sms, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "split-K fold launch");
+            return 0;
+        }
         e = launch_gemm_tc(type, w, s->xh, y, rows, cols, batch, rows, s->status, stream);
         if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
         return 0;
@@ -617,7 +636,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
-    const bool tc = batch >= kTensorCoreMinBatch && gemm_tc_supported(type, rows, cols, batch);
+    const bool tc = batch >= kTensorCoreMinBatch && cols >= kTensorCoreMinCols &&
+                    gemm_tc_supported(type, rows, cols, batch);
     if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
         const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, tokens);
@@ -648,8 +668,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
         }
     }
     if (tc) {
-        out[0] = 5;  // tcgen05 GEMM: 128-row x 256-token tiles
-        out[1] = gemm_tc_ctas(rows, batch);
+        out[0] = 5;  // tcgen05 GEMM: 256-row x 256-token tiles, K split over CTAs when tiles are few
+        out[1] = gemm_tc_ctas(rows, batch) * gemm_tc_splits(rows, cols, batch, s->num_sms);
         out[2] = 320;
         out[4] = 128;
         return 0;

@@ -149,6 +149,20 @@ def test_batched_matches_serial_reference(lib, cuda, oracle, t):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"batch item {b}")
 
 
+# Batches of 16+ vectors with rows shorter than 1024 elements stay on the exact
+# int8 kernel (8 tokens per launch).
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0])
+def test_large_batch_short_rows_int8(lib, cuda, oracle, t):
+    rows, cols, batch = 19200, 512, 16
+    assert lib.plan_info(t, rows, cols, batch)["path"] == 4
+    w = B.gen_weight(t, rows, cols, 81)
+    x = B.gen_x(cols, 81, batch=batch)
+    y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    ref = oracle.matvec_batch(t, rows, cols, w, x)
+    for b in range(batch):
+        assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
+
+
 # Batches of 2-15 quantised vectors run the int8 tensor-pipe kernel with 8, 4, 2
 # and 1 token vectors per launch (every weight unit read once per launch): each
 # vector must match the reference's serial matvec.  Shapes cover a ragged last
@@ -172,7 +186,10 @@ def test_small_batch_int8_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
 # matvecs.  Shapes cover ragged token tiles (tiles of 256), ragged row tiles
 # (128) and an odd number of 256-element weight chunks.
 @pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
-@pytest.mark.parametrize("rows,cols,batch", [(300, 2048, 16), (1000, 4096, 64), (129, 1280, 300)])
+# The first three shapes have few 256-row tiles, so their K is split over several
+# CTAs (partial sums folded in split order); the last has enough tiles for one
+# CTA per tile.
+@pytest.mark.parametrize("rows,cols,batch", [(300, 2048, 16), (1000, 4096, 64), (129, 1280, 300), (19200, 2048, 16)])
 def test_batched_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
     plan = lib.plan_info(t, rows, cols, batch)
     assert plan["path"] == 5, plan
