@@ -42,11 +42,13 @@
 // groups and y accumulates in group order; the same warp owns a tile in every
 // group).
 //
-// Two CTA shapes: 8 consumer warps within 113 KB of shared memory, so two CTAs
-// fit on an SM (with programmatic dependent launch the next matvec's CTA
-// streams its first units while this one computes), or a CTA that has the SM
-// alone with a deeper ring.  Every wait is bounded; a CTA-wide abort flag stops
-// every warp after the first timed-out wait.
+// CTA shape: one CTA per SM with up to 16 consumer warps and one producer
+// warp (96 registers; 8 consumer warps within 128 registers when several
+// token vectors share a launch) and a ring of up to 32 units in the whole
+// shared memory.  With programmatic dependent launch a CTA starts streaming its
+// weight as soon as the previous kernel's CTA on its SM exits, and reads x only
+// after that kernel has completed.  Every wait is bounded; a CTA-wide abort
+// flag stops every warp after the first timed-out wait.
 #include <math.h>
 
 #include "common.cuh"
