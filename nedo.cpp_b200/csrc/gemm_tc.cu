@@ -49,6 +49,13 @@ template <uint32_t TYPE>
 constexpr uint32_t stages() {
     return TYPE == kF16 ? 6u : 4u;
 }
+// X-tile stages: one more than the A stages for quantised weights (the X tiles
+// come from L2 and need the longer lead; the A tiles wait for the dequant warps
+// anyway); F16 loads A and X into the same stages.
+template <uint32_t TYPE>
+constexpr uint32_t stages_b() {
+    return TYPE == kF16 ? stages<TYPE>() : stages<TYPE>() + 1u;
+}
 constexpr uint32_t kRawSlots = 2;
 constexpr uint32_t kDeqWarps = 8;     // warps 2..9: dequant, then epilogue
 constexpr uint32_t kThreads = (2 + kDeqWarps) * 32;
@@ -257,15 +264,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* const sbase = smem_raw + (s0 - smem_addr(smem_raw));
     constexpr bool kRawW = TYPE != kF16;
     constexpr uint32_t kS = stages<TYPE>();
+    constexpr uint32_t kSB = stages_b<TYPE>();
     constexpr uint32_t kRawBytes = kRawW ? kRows * raw_row_bytes<TYPE>() : 0u;
     const uint32_t sA = s0;                       // kS x 16 KB (two 128-row halves)
-    const uint32_t sB = sA + kS * kStageA;        // kS x 16 KB
-    const uint32_t sRaw = sB + kS * kStageB;          // kRawSlots x raw chunk
+    const uint32_t sB = sA + kS * kStageA;        // kSB x 16 KB
+    const uint32_t sRaw = sB + kSB * kStageB;     // kRawSlots x raw chunk
     uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + (sRaw - s0) + kRawSlots * kRawBytes);
-    uint64_t* b_full = bars;                  // [kS] X (and F16 W) tiles landed
-    uint64_t* a_full = bars + kS;        // [kS] A tile written by the dequant warps
-    uint64_t* ab_empty = bars + 2 * kS;  // [kS] MMAs of the stage done
-    uint64_t* raw_full = bars + 3 * kS;  // [kRawSlots]
+    uint64_t* b_full = bars;                  // [kSB] X (and F16 W) tiles landed
+    uint64_t* a_full = b_full + kSB;          // [kS] A tile written by the dequant warps
+    uint64_t* ab_empty = a_full + kS;         // [kS] MMAs of the A stage (F16: the stage) done
+    uint64_t* b_empty = ab_empty + kS;        // [kSB] MMAs of the X stage done (quantised weights)
+    uint64_t* raw_full = b_empty + kSB;       // [kRawSlots]
     uint64_t* raw_empty = raw_full + kRawSlots;
     uint64_t* done = raw_empty + kRawSlots;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -284,9 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < kS; ++s) {
-            mbar_init(&b_full[s], 1);
             mbar_init(&a_full[s], kRawW ? kDeqWarps : 1u);
             mbar_init(&ab_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < kSB; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         for (uint32_t s = 0; s < kRawSlots; ++s) {
             mbar_init(&raw_full[s], 1);
@@ -300,6 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                      "r"(kHalves * kBN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    // every warp arrives converged: a CTA barrier counts a warp whose first
+    // lanes arrive while another lane still works as arrived
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -340,23 +355,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ks = kc * (kRawK / kBK) + j;
                     if (ks >= ks_end) break;
                     const uint32_t ls = ks - ks_begin;  // local k-step: stage and phase
-                    const uint32_t s = ls % kS;
-                    if (ls >= kS && !mbar_wait_bounded(&ab_empty[s], ((ls / kS) - 1u) & 1u, a.status, 32u)) {
+                    const uint32_t sb = ls % kSB;       // F16: kSB == kS, the stage of A and X
+                    uint64_t* freed = kRawW ? &b_empty[sb] : &ab_empty[sb];
+                    if (ls >= kSB && !mbar_wait_bounded(freed, ((ls / kSB) - 1u) & 1u, a.status, 32u)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&b_full[s], kStageB + (kRawW ? 0u : kStageA));
-                    tma_load_2d(sB + s * kStageB, &map_x, static_cast<int32_t>(ks * kBK), static_cast<int32_t>(tok0),
-                                &b_full[s]);
+                    mbar_arrive_expect_tx(&b_full[sb], kStageB + (kRawW ? 0u : kStageA));
+                    tma_load_2d(sB + sb * kStageB, &map_x, static_cast<int32_t>(ks * kBK),
+                                static_cast<int32_t>(tok0), &b_full[sb]);
                     if constexpr (!kRawW)
-                        tma_load_2d(sA + s * kStageA, &map_w, static_cast<int32_t>(ks * kBK),
-                                    static_cast<int32_t>(row0), &b_full[s]);
+                        tma_load_2d(sA + sb * kStageA, &map_w, static_cast<int32_t>(ks * kBK),
+                                    static_cast<int32_t>(row0), &b_full[sb]);
                     issued_ks = ls + 1u;
                 }
             }
             // drain: the last copies issued into every slot have landed before exit
-            for (uint32_t k = issued_ks > kS ? issued_ks - kS : 0u; k < issued_ks; ++k)
-                mbar_wait_bounded(&b_full[k % kS], (k / kS) & 1u, a.status, 38u);
+            for (uint32_t k = issued_ks > kSB ? issued_ks - kSB : 0u; k < issued_ks; ++k)
+                mbar_wait_bounded(&b_full[k % kSB], (k / kSB) & 1u, a.status, 38u);
             for (uint32_t k = issued_kc > kRawSlots ? issued_kc - kRawSlots : 0u; k < issued_kc; ++k)
                 mbar_wait_bounded(&raw_full[k % kRawSlots], (k / kRawSlots) & 1u, a.status, 39u);
         }
@@ -366,11 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (uint32_t ls = 0; ls < ks_end - ks_begin && ok; ++ls) {
                 const uint32_t s = ls % kS, ph = (ls / kS) & 1u;
-                ok = mbar_wait_bounded(&b_full[s], ph, a.status, 33u);
+                const uint32_t sb = ls % kSB, phb = (ls / kSB) & 1u;
+                ok = mbar_wait_bounded(&b_full[sb], phb, a.status, 33u);
                 if constexpr (kRawW) ok = ok && mbar_wait_bounded(&a_full[s], ph, a.status, 34u);
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t bd = sw64_desc(sB + s * kStageB);
+                const uint64_t bd = sw64_desc(sB + sb * kStageB);
 #pragma unroll
                 for (uint32_t h = 0; h < kHalves; ++h) {
                     const uint64_t ad = sw64_desc(sA + s * kStageA + h * (kBM * 64u));
@@ -379,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, kIdesc, (ls | kk) != 0u);
                 }
                 tc_commit(&ab_empty[s]);
+                if constexpr (kRawW) tc_commit(&b_empty[sb]);
             }
             tc_commit(done);  // every MMA issued above has completed when this arrives
         }
@@ -444,6 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
+    // lanes 1..31 of the producer and MMA warps wait here for lane 0, so the
+    // barrier below holds until every warp (the epilogue included) is done
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -502,7 +523,9 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     }
     constexpr uint32_t raw_bytes = TYPE == kF16 ? 0u : kRows * raw_row_bytes<TYPE>();
     constexpr uint32_t kS = stages<TYPE>();
-    const uint32_t smem = 1024u + kS * (kStageA + kStageB) + kRawSlots * raw_bytes + 8u * (3u * kS + 2u * kRawSlots + 1u) + 16u;
+    constexpr uint32_t kSB = stages_b<TYPE>();
+    const uint32_t smem = 1024u + kS * kStageA + kSB * kStageB + kRawSlots * raw_bytes +
+                          8u * (2u * kS + 2u * kSB + 2u * kRawSlots + 1u) + 16u;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

@@ -382,6 +382,7 @@ __global__ void __maxnreg__(NT == 1 ? 96 : 128)
         *abort_flag = 0u;
         fence_barrier_init();
     }
+    __syncwarp();  // warp 0 converged before the CTA barrier
     __syncthreads();
     // The next kernel on the stream may be scheduled now: its CTAs only stream
     // their weights until this grid has completed.

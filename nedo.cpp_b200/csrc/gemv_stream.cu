@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(const StreamArgs a)
                        &bars[t], policy);
         }
     }
+    __syncwarp();     // warp 0 converged (lane 0 issued the first tiles)
     __syncthreads();  // barrier initialisation visible to every warp
 
     grid_dependency_wait();  // x and y may be produced / consumed by earlier kernels
