@@ -24,6 +24,11 @@
 //     tcgen05.commit releases each stage.  The dequant warps then read TMEM
 //     (tcgen05.ld 32x32b) and store Y.
 //
+//   * Quantised weights with more than 256 tokens (and no K split) run on CTA
+//     pairs instead (gemm_tc_pair_kernel): tcgen05.mma.cta_group::2 with
+//     M = 256 across the pair and each SM holding half of every token tile,
+//     which cuts the shared-memory bytes per MMA that bound the one-SM tile.
+//
 // fp16 rounding of x and of d*q is the only difference from the reference's
 // fp32 arithmetic (relative 2^-11 per factor); the products are summed in fp32.
 // Every wait is bounded; TMEM is released on every path.
@@ -558,6 +563,369 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TYPE>, mw, mx, a);
 }
 
+// ---- 2-SM variant (quantised weights, more than 256 tokens) ---------------
+// A cluster of two CTAs computes a tile of 256 weight rows x 512 tokens with
+// tcgen05.mma.cta_group::2 (M = 256 across the pair, N = 256 per MMA, two token
+// halves).  CTA rank r holds rows 128r..128r+127 of A and tokens
+// 128r..128r+127 of each token half of B, so each SM's MMAs read half of the
+// B bytes a one-SM tile of the same work would: shared-memory traffic per K
+// stage drops from ~97 KB to ~65 KB per SM.  The leader (rank 0) issues the
+// MMAs; the X copies of both CTAs and the dequant warps of both CTAs signal
+// the leader's barriers; its commits reach both CTAs.  Raw weight chunks stay
+// per CTA.  Each CTA's TMEM holds its 128 rows of both 256-token accumulators.
+namespace pair {
+constexpr uint32_t kRowsC = 128;             // weight rows per CTA (pair: 256)
+constexpr uint32_t kTokC = 128;              // tokens per CTA per token half
+constexpr uint32_t kTokPair = 512;           // tokens per pair tile (two MMA N = 256 halves)
+constexpr uint32_t kS = 6;                   // A stages
+constexpr uint32_t kSB = 6;                  // X stages
+// raw chunk slots: every weight row is read by one CTA only (no second token
+// tile hits it in L2), so the chunks are fetched four ahead
+constexpr uint32_t kRawSlotsP = 4;
+constexpr uint32_t kPairStageA = kRowsC * 64;    // 8 KB
+constexpr uint32_t kHalfB = kTokC * 64;      // 8 KB: one token half
+constexpr uint32_t kPairStageB = 2 * kHalfB;     // 16 KB
+constexpr uint32_t kXBytesPair = 2 * kPairStageB;  // bytes landing on the leader's X barrier per stage
+// kind::f16, fp32 D, M = 256 (pair), N = 256
+constexpr uint32_t kIdesc2 = (1u << 4) | ((256u >> 3) << 17) | ((256u >> 4) << 24);
+
+template <uint32_t TYPE>
+constexpr uint32_t raw_bytes() { return kRowsC * raw_row_bytes<TYPE>(); }
+template <uint32_t TYPE>
+constexpr uint32_t smem_bytes() {
+    return 1024u + kS * kPairStageA + kSB * kPairStageB + kRawSlotsP * raw_bytes<TYPE>() +
+           8u * (2u * kS + 2u * kSB + 2u * kRawSlotsP + 1u) + 16u;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// X copy into this CTA's shared memory, completion on a barrier of either CTA of the pair
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cluster_addr) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster_addr)
+        : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate)
+        : "memory");
+}
+// arrive on the barrier at this offset in both CTAs once the MMAs issued so far complete
+__device__ __forceinline__ void commit_both(uint64_t* bar) {
+    const uint16_t mask = 3;
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                     "r"(smem_addr(bar)),
+                 "h"(mask)
+                 : "memory");
+}
+// bounded wait.  Most phases of this kernel's barriers are completed from the
+// other SM of the pair (remote arrivals, the peer's copies, multicast
+// commits), so the wait takes no suspend-time hint.
+__device__ __forceinline__ bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool wait_cluster_bounded(uint64_t* bar, uint32_t parity, DeviceStatus* st, uint32_t site) {
+    if (try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (try_wait_cluster(bar, parity)) return true;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (st != nullptr && atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
+            return false;
+        }
+    }
+}
+}  // namespace pair
+
+template <uint32_t TYPE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                        const GemmArgs a) {
+    using namespace pair;
+    static_assert(TYPE != kF16, "the pair kernel dequantises GGUF blocks");
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t s0 = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    uint8_t* const sbase = smem_raw + (s0 - smem_addr(smem_raw));
+    constexpr uint32_t kRawB = raw_bytes<TYPE>();
+    const uint32_t sA = s0;                        // kS x 8 KB
+    const uint32_t sB = sA + kS * kPairStageA;         // kSB x 16 KB (two token halves)
+    const uint32_t sRaw = sB + kSB * kPairStageB;      // kRawSlotsP x raw chunk
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sbase + (sRaw - s0) + kRawSlotsP * kRawB);
+    uint64_t* b_full = bars;                  // [kSB] leader: X of both CTAs landed
+    uint64_t* a_full = b_full + kSB;          // [kS] leader: A written by both CTAs' dequant warps
+    uint64_t* a_empty = a_full + kS;          // [kS] both: MMAs of the A stage done
+    uint64_t* b_empty = a_empty + kS;         // [kSB] both: MMAs of the X stage done
+    uint64_t* raw_full = b_empty + kSB;       // [kRawSlotsP] per CTA
+    uint64_t* raw_empty = raw_full + kRawSlotsP;
+    uint64_t* done = raw_empty + kRawSlotsP;   // both: every MMA complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_rank();
+    const uint32_t row0 = (blockIdx.x >> 1) * (2u * kRowsC) + rank * kRowsC;  // this CTA's weight rows
+    const uint32_t tok0 = blockIdx.y * kTokPair;                             // the pair's tokens
+    const uint32_t ksteps = (a.cols + kBK - 1) / kBK;
+    const uint32_t chunks = (a.cols + kRawK - 1) / kRawK;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < kS; ++s) {
+            mbar_init(&a_full[s], 2u * 4u);  // 4 dequant warps of each CTA write a stage
+            mbar_init(&a_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < kSB; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (uint32_t s = 0; s < kRawSlotsP; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], kDeqWarps);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM: both token halves, 2 x 256 fp32 columns (same warp in both CTAs)
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(2u * kBN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    __syncwarp();
+    tc_fence_before();
+    // both CTAs' barriers are initialised before either signals the other's
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            uint32_t issued_ks = 0, issued_kc = 0;
+            bool ok = true;
+            auto load_raw = [&](uint32_t kc) {
+                const uint32_t rs = kc % kRawSlotsP;
+                mbar_arrive_expect_tx(&raw_full[rs], kRawB);
+                const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
+                tma_load_2d(sRaw + rs * kRawB, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
+                            static_cast<int32_t>(row0), &raw_full[rs]);
+                issued_kc = kc + 1u;
+            };
+            for (uint32_t kc = 0; kc < kRawSlotsP && kc < chunks; ++kc) load_raw(kc);
+            grid_dependency_wait();  // X may come from the previous kernel
+            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
+                if (kc >= kRawSlotsP) {
+                    if (!pair::wait_cluster_bounded(&raw_empty[kc % kRawSlotsP], ((kc / kRawSlotsP) - 1u) & 1u, a.status, 51u)) {
+                        ok = false;
+                        break;
+                    }
+                    load_raw(kc);
+                }
+                for (uint32_t j = 0; j < kRawK / kBK; ++j) {
+                    const uint32_t ks = kc * (kRawK / kBK) + j;
+                    if (ks >= ksteps) break;
+                    const uint32_t sb = ks % kSB;
+                    if (ks >= kSB && !pair::wait_cluster_bounded(&b_empty[sb], ((ks / kSB) - 1u) & 1u, a.status, 52u)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&b_full[sb], kXBytesPair);
+                    const uint32_t bar = map_to_rank(smem_addr(&b_full[sb]), 0);
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h)  // token half h: tokens 256h + 128 rank ..
+                        tma_load_2d_pair(sB + sb * kPairStageB + h * kHalfB, &map_x, static_cast<int32_t>(ks * kBK),
+                                         static_cast<int32_t>(tok0 + h * kBN + rank * kTokC), bar);
+                    issued_ks = ks + 1u;
+                }
+            }
+            // drain: this CTA's raw copies; the leader also waits for the last X
+            // stages, whose barrier counts the peer's copies too
+            if (rank == 0)
+                for (uint32_t k = issued_ks > kSB ? issued_ks - kSB : 0u; k < issued_ks; ++k)
+                    pair::wait_cluster_bounded(&b_full[k % kSB], (k / kSB) & 1u, a.status, 58u);
+            for (uint32_t k = issued_kc > kRawSlotsP ? issued_kc - kRawSlotsP : 0u; k < issued_kc; ++k)
+                pair::wait_cluster_bounded(&raw_full[k % kRawSlotsP], (k / kRawSlotsP) & 1u, a.status, 59u);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader only) ----------------
+        if (rank == 0 && lane == 0) {
+            bool ok = true;
+            for (uint32_t ks = 0; ks < ksteps && ok; ++ks) {
+                const uint32_t s = ks % kS, sb = ks % kSB;
+                ok = wait_cluster_bounded(&b_full[sb], (ks / kSB) & 1u, a.status, 53u) &&
+                     wait_cluster_bounded(&a_full[s], (ks / kS) & 1u, a.status, 54u);
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t ad = sw64_desc(sA + s * kPairStageA);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint64_t bd = sw64_desc(sB + sb * kPairStageB + h * kHalfB);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // +32 bytes = +2 in descriptor units
+                        mma_pair(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, (ks | kk) != 0u);
+                }
+                commit_both(&a_empty[s]);
+                commit_both(&b_empty[sb]);
+            }
+            commit_both(done);
+        }
+    } else {
+        // ---------------- dequant warps (both CTAs), then the epilogue ----------------
+        // warps 2..5 write the even K stages of a chunk, warps 6..9 the odd ones;
+        // one thread per row of this CTA's 128
+        const uint32_t t = threadIdx.x - 64u;
+        const uint32_t r = t & (kRowsC - 1u);
+        const uint32_t grp = t >> 7;
+        bool ok = true;
+        for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
+            const uint32_t rs = kc % kRawSlotsP;
+            if (!pair::wait_cluster_bounded(&raw_full[rs], (kc / kRawSlotsP) & 1u, a.status, 55u)) {
+                ok = false;
+                break;
+            }
+            const uint32_t raw_row = sRaw + rs * kRawB + r * raw_row_bytes<TYPE>();
+            auto stage = [&](auto J) {
+                constexpr uint32_t j = decltype(J)::value;
+                const uint32_t ks = kc * (kRawK / kBK) + j;
+                if (!ok || ks >= ksteps) return;
+                const uint32_t s = ks % kS;
+                if (ks >= kS && !pair::wait_cluster_bounded(&a_empty[s], ((ks / kS) - 1u) & 1u, a.status, 56u)) {
+                    ok = false;
+                    return;
+                }
+                if (kc & 1u)  // odd chunks start 8 bytes into the loaded row
+                    dequant_block<TYPE, 8u, j>(raw_row, sA + s * kPairStageA, r);
+                else
+                    dequant_block<TYPE, 0u, j>(raw_row, sA + s * kPairStageA, r);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
+                __syncwarp();
+                if (lane == 0) arrive_remote(map_to_rank(smem_addr(&a_full[s]), 0));
+            };
+            if (grp == 0) {
+                stage(Idx<0>{});
+                stage(Idx<2>{});
+            } else {
+                stage(Idx<1>{});
+                stage(Idx<3>{});
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        }
+        // epilogue: warp w reads TMEM lane quarter w % 4 of token half (w - 2) / 4
+        const uint32_t quarter = warp & 3u;
+        const uint32_t h = (warp - 2u) >> 2;
+        if (pair::wait_cluster_bounded(done, 0, a.status, 57u)) {
+            tc_fence_after();
+            const uint32_t wrow = row0 + quarter * 32u + lane;
+            for (uint32_t col = 0; col < kBN; col += 32u) {
+                uint32_t v[32];
+                tc_ld_32x32b_x32(tmem_d + h * kBN + ((quarter * 32u) << 16) + col, v);
+                if (wrow < a.rows) {
+#pragma unroll
+                    for (uint32_t i = 0; i < 32; ++i) {
+                        const uint32_t tk = tok0 + h * kBN + col + i;
+                        if (tk < a.tokens) a.y[static_cast<size_t>(tk) * a.ldy + wrow] = __uint_as_float(v[i]);
+                    }
+                }
+            }
+        }
+    }
+    // every warp converged; both CTAs done with TMEM and with each other's barriers
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(2u * kBN));
+    }
+}
+
+
+template <uint32_t TYPE>
+cudaError_t launch_pair_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
+                          uint32_t ldy, DeviceStatus* status, cudaStream_t stream) {
+    EncodeTiled enc = encode_tiled_fn();
+    if (enc == nullptr) return cudaErrorNotSupported;
+    CUtensorMap mw, mx;
+    const uint64_t rb = row_bytes_of(TYPE, cols);
+    {
+        // raw rows as uint16 elements, 128 rows per box (one CTA's share of the pair)
+        const cuuint64_t dims[2] = {rb / 2u, rows}, strides[1] = {rb};
+        const cuuint32_t box[2] = {raw_row_bytes<TYPE>() / 2u, pair::kRowsC}, es[2] = {1, 1};
+        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        const cuuint64_t dims[2] = {cols, tokens}, strides[1] = {static_cast<cuuint64_t>(cols) * 2u};
+        const cuuint32_t box[2] = {kBK, pair::kTokC}, es[2] = {1, 1};
+        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(xh), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_tc_pair_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             pair::smem_bytes<TYPE>());
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    GemmArgs a{};
+    a.y = y;
+    a.rows = rows;
+    a.cols = cols;
+    a.tokens = tokens;
+    a.ldy = ldy;
+    a.ksplit = 1;
+    a.split_stride = 0;
+    a.status = status;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2u * ((rows + 2u * pair::kRowsC - 1) / (2u * pair::kRowsC)),
+                       (tokens + pair::kTokPair - 1) / pair::kTokPair, 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pair::smem_bytes<TYPE>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<TYPE>, mw, mx, a);
+}
+
+// Quantised weights with more than one 256-token tile and no K split run on
+// CTA pairs.
+bool use_pair(uint32_t type, uint64_t tokens, uint32_t ksplit) { return type != kF16 && tokens > kBN && ksplit == 1; }
+
 }  // namespace
 
 EncodeTiled encode_tiled_fn() {
@@ -583,6 +951,14 @@ bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tok
 
 uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens) {
     return static_cast<uint32_t>(((rows + kRows - 1) / kRows) * ((tokens + kBN - 1) / kBN));
+}
+
+uint32_t gemm_tc_launch_ctas(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms) {
+    const uint32_t splits = gemm_tc_splits(rows, cols, tokens, num_sms);
+    if (use_pair(type, tokens, splits))
+        return static_cast<uint32_t>(2u * ((rows + 2u * pair::kRowsC - 1) / (2u * pair::kRowsC)) *
+                                     ((tokens + pair::kTokPair - 1) / pair::kTokPair));
+    return gemm_tc_ctas(rows, tokens) * splits;
 }
 
 uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms) {
@@ -628,6 +1004,10 @@ cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float
     if (!gemm_tc_supported(type, rows, cols, tokens)) return cudaErrorInvalidValue;
     if (ksplit == 0 || ksplit > (cols + kRawK - 1) / kRawK || ksplit > 65535u) return cudaErrorInvalidValue;
     const uint32_t r = static_cast<uint32_t>(rows), c = static_cast<uint32_t>(cols), t = static_cast<uint32_t>(tokens);
+    if (use_pair(type, tokens, ksplit)) {
+        if (type == kQ8_0) return launch_pair_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        return launch_pair_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+    }
     switch (type) {
         case kQ8_0:
             return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);

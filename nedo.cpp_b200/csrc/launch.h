@@ -135,6 +135,10 @@ cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float
                            uint32_t ksplit = 1, uint64_t split_stride = 0);
 // CTAs along K per tile for a GEMM whose tiles would leave most SMs idle (1 otherwise).
 uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms);
+// CTAs launch_gemm_tc starts for this shape with gemm_tc_splits' K split: quantised
+// weights with more than 256 tokens and no split run as CTA pairs of 256 rows x
+// 512 tokens, everything else as 256-row x 256-token tiles.
+uint32_t gemm_tc_launch_ctas(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms);
 // y[t * ldy + r] = sum_z ws[(z * tokens + t) * rows + r], z in order (deterministic).
 cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uint64_t tokens, uint64_t rows,
                                  uint64_t ldy, int num_sms, cudaStream_t stream);

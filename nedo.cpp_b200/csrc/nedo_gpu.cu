@@ -669,7 +669,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     }
     if (tc) {
         out[0] = 5;  // tcgen05 GEMM: 256-row x 256-token tiles, K split over CTAs when tiles are few
-        out[1] = gemm_tc_ctas(rows, batch) * gemm_tc_splits(rows, cols, batch, s->num_sms);
+        out[1] = gemm_tc_launch_ctas(type, rows, cols, batch, s->num_sms);
         out[2] = 320;
         out[4] = 128;
         return 0;

@@ -201,6 +201,26 @@ def test_batched_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batc
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
 
 
+# Quantised batches of more than 256 tokens run on CTA pairs (256 rows x 512
+# tokens per pair, tcgen05 MMAs with M = 256 across the two SMs).  9500 rows
+# end inside a pair (the second CTA of the last pair has 32 rows); 520 tokens
+# leave a second pair tile with 8 tokens.
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0])
+@pytest.mark.parametrize("rows,cols,batch", [(9500, 1024, 300), (8000, 1024, 520)])
+def test_pair_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
+    plan = lib.plan_info(t, rows, cols, batch)
+    assert plan["path"] == 5, plan
+    assert plan["grid"] == 2 * ((rows + 255) // 256) * ((batch + 511) // 512), plan
+    w = B.gen_weight(t, rows, cols, 61 + batch)
+    x = B.gen_x(cols, 61 + batch, batch=batch)
+    y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    again = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    assert np.array_equal(y.view(np.uint32), again.view(np.uint32))
+    ref = oracle.matvec_batch(t, rows, cols, w, x)
+    for b in range(batch):
+        assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
+
+
 def test_lm_head_argmax(lib, cuda, oracle):
     # F16 LM head with the greedy pick fused into the matvec kernel.
     rows, cols = 32000, 2048
