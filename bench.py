@@ -97,7 +97,7 @@ NCU_TRAFFIC_BYTES = {
     "q8_0_4096x4096": 17_893_632,
     "q4_0_32768x32768": 609_625_344,
     "f16_head_128000x2048": 527_622_400,
-    "q8_0_prefill_512x4096x14336": 70_580_992,
+    "q8_0_prefill_512x4096x14336": 70_827_776,
 }
 
 
