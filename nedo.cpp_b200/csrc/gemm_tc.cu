@@ -724,52 +724,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem_d = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer (both CTAs) ----------------
-        if (lane == 0) {
-            uint32_t issued_ks = 0, issued_kc = 0;
-            bool ok = true;
-            auto load_raw = [&](uint32_t kc) {
+        // ---------------- TMA producers (both CTAs) ----------------
+        // lane 1 streams this CTA's raw weight chunks, gated only by free raw
+        // slots (weights never come from the previous kernel), so they are
+        // fetched kRawSlotsP chunks ahead; lane 0 copies the X tiles, gated by
+        // the MMAs freeing X stages
+        if (lane == 1) {
+            uint32_t issued_kc = 0;
+            for (uint32_t kc = 0; kc < chunks; ++kc) {
                 const uint32_t rs = kc % kRawSlotsP;
+                if (kc >= kRawSlotsP &&
+                    !pair::wait_cluster_bounded(&raw_empty[rs], ((kc / kRawSlotsP) - 1u) & 1u, a.status, 51u))
+                    break;
                 mbar_arrive_expect_tx(&raw_full[rs], kRawB);
+                // the chunk's first byte, rounded down to 16 bytes (uint16 elements)
                 const uint32_t first = kc * (kRawK / 32u) * RawBlock<TYPE>::kBytes;
                 tma_load_2d(sRaw + rs * kRawB, &map_w, static_cast<int32_t>((first & ~15u) / 2u),
                             static_cast<int32_t>(row0), &raw_full[rs]);
                 issued_kc = kc + 1u;
-            };
-            for (uint32_t kc = 0; kc < kRawSlotsP && kc < chunks; ++kc) load_raw(kc);
-            grid_dependency_wait();  // X may come from the previous kernel
-            for (uint32_t kc = 0; kc < chunks && ok; ++kc) {
-                if (kc >= kRawSlotsP) {
-                    if (!pair::wait_cluster_bounded(&raw_empty[kc % kRawSlotsP], ((kc / kRawSlotsP) - 1u) & 1u, a.status, 51u)) {
-                        ok = false;
-                        break;
-                    }
-                    load_raw(kc);
-                }
-                for (uint32_t j = 0; j < kRawK / kBK; ++j) {
-                    const uint32_t ks = kc * (kRawK / kBK) + j;
-                    if (ks >= ksteps) break;
-                    const uint32_t sb = ks % kSB;
-                    if (ks >= kSB && !pair::wait_cluster_bounded(&b_empty[sb], ((ks / kSB) - 1u) & 1u, a.status, 52u)) {
-                        ok = false;
-                        break;
-                    }
-                    if (rank == 0) mbar_arrive_expect_tx(&b_full[sb], kXBytesPair);
-                    const uint32_t bar = map_to_rank(smem_addr(&b_full[sb]), 0);
-#pragma unroll
-                    for (uint32_t h = 0; h < 2; ++h)  // token half h: tokens 256h + 128 rank ..
-                        tma_load_2d_pair(sB + sb * kPairStageB + h * kHalfB, &map_x, static_cast<int32_t>(ks * kBK),
-                                         static_cast<int32_t>(tok0 + h * kBN + rank * kTokC), bar);
-                    issued_ks = ks + 1u;
-                }
             }
-            // drain: this CTA's raw copies; the leader also waits for the last X
-            // stages, whose barrier counts the peer's copies too
+            // drain: the last raw copies have landed before exit
+            for (uint32_t k = issued_kc > kRawSlotsP ? issued_kc - kRawSlotsP : 0u; k < issued_kc; ++k)
+                pair::wait_cluster_bounded(&raw_full[k % kRawSlotsP], (k / kRawSlotsP) & 1u, a.status, 59u);
+        } else if (lane == 0) {
+            uint32_t issued_ks = 0;
+            grid_dependency_wait();  // X may come from the previous kernel
+            for (uint32_t ks = 0; ks < ksteps; ++ks) {
+                const uint32_t sb = ks % kSB;
+                if (ks >= kSB && !pair::wait_cluster_bounded(&b_empty[sb], ((ks / kSB) - 1u) & 1u, a.status, 52u))
+                    break;
+                if (rank == 0) mbar_arrive_expect_tx(&b_full[sb], kXBytesPair);
+                const uint32_t bar = map_to_rank(smem_addr(&b_full[sb]), 0);
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h)  // token half h: tokens 256h + 128 rank ..
+                    tma_load_2d_pair(sB + sb * kPairStageB + h * kHalfB, &map_x, static_cast<int32_t>(ks * kBK),
+                                     static_cast<int32_t>(tok0 + h * kBN + rank * kTokC), bar);
+                issued_ks = ks + 1u;
+            }
+            // drain: the leader waits for the last X stages, whose barrier also
+            // counts the peer's copies
             if (rank == 0)
                 for (uint32_t k = issued_ks > kSB ? issued_ks - kSB : 0u; k < issued_ks; ++k)
                     pair::wait_cluster_bounded(&b_full[k % kSB], (k / kSB) & 1u, a.status, 58u);
-            for (uint32_t k = issued_kc > kRawSlotsP ? issued_kc - kRawSlotsP : 0u; k < issued_kc; ++k)
-                pair::wait_cluster_bounded(&raw_full[k % kRawSlotsP], (k / kRawSlotsP) & 1u, a.status, 59u);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader only) ----------------
