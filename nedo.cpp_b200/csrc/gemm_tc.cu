@@ -247,6 +247,8 @@ struct Idx {
 __global__ void x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ xh, uint64_t n) {
     // the GEMM that reads xh may launch now: it streams its weights until this grid completes
     asm volatile("griddepcontrol.launch_dependents;");
+    // launched early itself: x may come from, and xh is read by, the kernels before
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (uint64_t i = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) * 4u; i < n;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x * 4u) {
         if (i + 4u <= n) {
@@ -324,6 +326,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_d = *tmem_slot;
+    // the kernel after this one (the split-K fold, or the next conversion of x)
+    // may be scheduled now; it waits for this grid's completion before its work
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;");
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -482,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // by the GEMM launched just before, so the fold waits for that kernel first.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __restrict__ y, uint32_t splits,
                                      uint32_t tokens, uint32_t rows, uint64_t ldy) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the next kernel may be scheduled
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint64_t n = static_cast<uint64_t>(tokens) * rows;
     const uint64_t zstride = n;
@@ -990,8 +996,18 @@ cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms,
     uint64_t blocks = (n / 4u + 255u) / 256u;
     if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
     if (blocks == 0) blocks = 1;
-    x_to_f16_kernel<<<static_cast<uint32_t>(blocks), 256, 0, stream>>>(x, xh, n);
-    return cudaGetLastError();
+    // programmatic dependent launch: scheduled while the previous kernel runs,
+    // the conversion itself starts after that kernel's completion
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<uint32_t>(blocks));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, x_to_f16_kernel, x, xh, n);
 }
 
 cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
