@@ -218,6 +218,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // row, and rows of 1024 elements and more keep them inside 1e-4 * sum|w*x| on
 // the test distributions.  Shorter rows use the exact int8 kernel.
 constexpr uint32_t kTensorCoreMinBatch = 16;
+// F16 weights are exact in the GEMM (only x is rounded), and the alternative is
+// one streaming pass over the weight per token vector: from 4 vectors on one
+// GEMM pass is cheaper (an F16 64000x1536 head at 8 vectors: ~43 us against
+// 8 x 30 us).
+constexpr uint32_t kTensorCoreMinBatchF16 = 4;
+
+uint32_t tensor_core_min_batch(uint32_t type) { return type == kF16 ? kTensorCoreMinBatchF16 : kTensorCoreMinBatch; }
 constexpr uint64_t kTensorCoreMinCols = 1024;
 
 // The one dispatch point for every matvec launch.
@@ -241,7 +248,7 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             return 0;
         }
     }
-    if (batch >= kTensorCoreMinBatch && cols >= kTensorCoreMinCols && amax == nullptr && aligned16(w) &&
+    if (batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols && amax == nullptr && aligned16(w) &&
         aligned16(x) && gemm_tc_supported(type, rows, cols, batch)) {
         // tokens as the N dimension of a tcgen05 GEMM (x rounded to fp16 once)
         const uint64_t n = static_cast<uint64_t>(batch) * cols;
@@ -636,7 +643,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
-    const bool tc = batch >= kTensorCoreMinBatch && cols >= kTensorCoreMinCols &&
+    const bool tc = batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols &&
                     gemm_tc_supported(type, rows, cols, batch);
     if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
         const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;

@@ -221,6 +221,20 @@ def test_pair_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
 
 
+# F16 weights go to the tensor-core GEMM from 4 token vectors on (only x is
+# rounded to fp16 there); 3 vectors still stream the weight once per vector.
+@pytest.mark.parametrize("rows,cols,batch", [(2000, 1536, 5), (300, 2048, 4), (640, 1024, 3)])
+def test_f16_small_batch_vs_reference(lib, cuda, oracle, rows, cols, batch):
+    t = B.F16
+    assert (lib.plan_info(t, rows, cols, batch)["path"] == 5) == (batch >= 4)
+    w = B.gen_weight(t, rows, cols, 71 + batch)
+    x = B.gen_x(cols, 71 + batch, batch=batch)
+    y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    ref = oracle.matvec_batch(t, rows, cols, w, x)
+    for b in range(batch):
+        assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
+
+
 def test_lm_head_argmax(lib, cuda, oracle):
     # F16 LM head with the greedy pick fused into the matvec kernel.
     rows, cols = 32000, 2048
