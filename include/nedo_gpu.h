@@ -117,9 +117,12 @@ NEDO_GPU_API int nedo_gpu_cache_clear(void);
  * vectors: y_dev[b][r] = dot(row r, x_dev[b]), b < batch.  batch == 1 is the
  * decode path (src/model.cpp:217-259); batch > 1 replaces `batch` serial
  * calls over the same weight, which is how the reference processes a prompt
- * (src/model.cpp:262-266).  From 16 vectors on, the batch runs as one
- * tensor-core GEMM with x and the dequantised weight rounded to fp16 (fp32
- * accumulation); the first such call on a device allocates an fp16 copy of x. */
+ * (src/model.cpp:262-266).  For rows of at least 1024 elements, from 16
+ * vectors on (4 for F16 weights) the batch runs as one tensor-core GEMM with x
+ * and the dequantised weight rounded to fp16 (fp32 accumulation); the first
+ * such call on a device allocates an fp16 copy of x and, for few row tiles, a
+ * split-K workspace.  Such calls on one device share these buffers:
+ * serialise calls that may overlap (other streams, other threads). */
 NEDO_GPU_API int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
                         float* y_dev, uint32_t batch, void* stream);
 
