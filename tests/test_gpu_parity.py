@@ -196,6 +196,10 @@ def test_batched_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batc
     w = B.gen_weight(t, rows, cols, 31 + batch)
     x = B.gen_x(cols, 31 + batch, batch=batch)
     y = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    # a second call agrees bit for bit (split-K folds in split order, and its
+    # arrival counters are back at zero after every launch)
+    again = run_dev(lib, cuda, t, rows, cols, w, x, batch=batch)
+    assert np.array_equal(y.view(np.uint32), again.view(np.uint32))
     ref = oracle.matvec_batch(t, rows, cols, w, x)
     for b in range(batch):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"token {b}")
