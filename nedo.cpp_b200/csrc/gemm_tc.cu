@@ -493,8 +493,17 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __rest
     const uint64_t zstride = n;
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        float v = ws[i];
-        for (uint32_t z = 1; z < splits; ++z) v += ws[z * zstride + i];
+        // eight splits' loads in flight at a time, added in split order
+        float v = __ldg(ws + i);
+        uint32_t z = 1;
+        for (; z + 8u <= splits; z += 8u) {
+            float p[8];
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k) p[k] = __ldg(ws + (z + k) * zstride + i);
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k) v += p[k];
+        }
+        for (; z < splits; ++z) v += __ldg(ws + z * zstride + i);
         const uint64_t t = i / rows, r = i - t * rows;
         y[t * ldy + r] = v;
     }
