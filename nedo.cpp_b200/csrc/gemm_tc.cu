@@ -153,8 +153,9 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
     return d;
 }
 
-// kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M x N.
-constexpr uint32_t kIdesc = (1u << 4) | ((kBN >> 3) << 17) | ((kBM >> 4) << 24);
+// kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M = 128 x N
+// (N a multiple of 16, 16..256).
+__host__ __device__ constexpr uint32_t idesc_m128(uint32_t n) { return (1u << 4) | ((n >> 3) << 17) | ((kBM >> 4) << 24); }
 
 // fp16 tile element (row r, 16-byte chunk c of its 64-byte row) in the
 // 64-byte-swizzled K-major layout: byte-address bits 4-5 are XORed with bits
@@ -390,6 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             bool ok = true;
+            // MMA N: the tile's tokens rounded up to 16 (a batch of 32 computes 32
+            // accumulator columns, not 256; the epilogue never reads past them)
+            const uint32_t ntok = a.tokens - tok0 < kBN ? a.tokens - tok0 : kBN;
+            const uint32_t idesc = idesc_m128((ntok + 15u) & ~15u);
             for (uint32_t ls = 0; ls < ks_end - ks_begin && ok; ++ls) {
                 const uint32_t s = ls % kS, ph = (ls / kS) & 1u;
                 const uint32_t sb = ls % kSB, phb = (ls / kSB) & 1u;
@@ -403,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t ad = sw64_desc(sA + s * kStageA + h * (kBM * 64u));
 #pragma unroll
                     for (uint32_t kk = 0; kk < kBK / 16u; ++kk)  // K = 16 per MMA: 32 bytes along the row
-                        tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, kIdesc, (ls | kk) != 0u);
+                        tc_mma_f16(tmem_d + h * kBN, ad + 2u * kk, bd + 2u * kk, idesc, (ls | kk) != 0u);
                 }
                 tc_commit(&ab_empty[s]);
                 if constexpr (kRawW) tc_commit(&b_empty[sb]);
