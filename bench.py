@@ -30,14 +30,21 @@ Workloads (default q4_0_11008x4096):
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max over
-ranks.  The K steps run as one CUDA graph (at N>1 with the NCCL all-gather of
-each step inside it).  Weight copies rotate so the
-rotating set exceeds 4x L2 (each step reads a weight that is not in L2).
+ranks.  The K steps run as one CUDA graph (at N>1 with the all-gather of each
+step inside it).  Weight copies rotate so the rotating set exceeds 4x L2 (each
+step reads a weight that is not in L2).
+
+At N=1 the line also carries `workloads`: every other configuration above
+measured the same way in the same run (value, roofline fraction, clocks), and
+at N>1 `sharded`: the row-sharded Q4_0 32768x32768 step with its time split
+into the matvec and the gather wait.
 
 `e2e` repeats the metric through the host entry point of the C ABI
 (nedo_gpu_matvec: host x in, host y out, copies inside the timed region).
 `cpu_baseline` times the reference's own CPU kernel (compiled from source into
-oracle/_ref; the C restatement when that library is absent) on this host.
+oracle/_ref; the C restatement when that library is absent) on this host, and
+as the checker of the same leg compares one output of each measured GPU
+workload with the reference (`parity`).
 `--impl reference` times that same CPU kernel as the whole step.
 """
 from __future__ import annotations
@@ -49,6 +56,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -62,6 +70,7 @@ METRIC = "Q8_0/Q4_0/F16 matvec HBM GB/s & % of B200 peak; prefill GEMM TFLOP/s @
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1400.0
+TOL = 1e-4  # |y_gpu - y_ref| <= TOL * sum_i |w_i x_i| per output
 
 WORKLOADS = {
     "q4_0_11008x4096": dict(type=B.Q4_0, rows=11008, cols=4096, shard="replica", argmax=False),
@@ -75,6 +84,9 @@ for _b in (1, 8, 32):
     WORKLOADS[f"decode_sweep_24x1536_b{_b}"] = dict(kind="sweep", type=B.Q8_0, layers=24, d=1536, ff=4096,
                                                     head=64000, batch=_b, shard="replica", argmax=_b == 1,
                                                     rows=1536, cols=1536)
+# measured beside the default line at N=1 (every configuration of the path)
+SIDE_WORKLOADS = ["q8_0_4096x4096", "f16_head_128000x2048", "q4_0_32768x32768", "q8_0_prefill_512x4096x14336",
+                  "decode_sweep_24x1536_b1", "decode_sweep_24x1536_b8", "decode_sweep_24x1536_b32"]
 
 
 def sweep_matrices(wl):
@@ -88,6 +100,7 @@ def sweep_matrices(wl):
 def sweep_bytes(wl, batch):
     """Algorithmic bytes of one step: every weight once, x and y per token."""
     return sum(r * B.row_bytes(t, c) + batch * 4 * (r + c) for _, t, r, c in sweep_matrices(wl))
+
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
 # capture of the same workload (dram__bytes_read.sum + dram__bytes_write.sum);
@@ -153,6 +166,35 @@ def work_of(wl, rows_total, batch=None):
     return float(algorithmic_bytes(wl["type"], rows_total, wl["cols"])), "GB/s", 1e9
 
 
+def workload_config(name, wl, world):
+    """The `config` of a line: identical in both arms (implementation details go to `setup`)."""
+    if wl.get("kind") == "sweep":
+        return {"workload": name,
+                "description": f"{wl['layers']}-layer d_model {wl['d']} decoder step: "
+                               f"{len(sweep_matrices(wl)) - 1} Q8_0 matvecs + F16 {wl['head']}x{wl['d']} head, "
+                               f"{batch_of(wl)} token(s) per step",
+                "batch": batch_of(wl), "weight_bytes_per_step": sum(r * B.row_bytes(t, c)
+                                                                    for _, t, r, c in sweep_matrices(wl)),
+                "parallelism": "replicas" if world > 1 else "single"}
+    rows, rows_total = shard_rows(wl, world)
+    t = B.TYPE_NAMES[wl["type"]]
+    desc = f"{t} matvec {rows_total}x{wl['cols']} batch {batch_of(wl)}"
+    if batch_of(wl) > 1:
+        desc = (f"{t} {wl['rows']}x{wl['cols']} weight x {batch_of(wl)} token vectors "
+                f"(prefill GEMM, M={batch_of(wl)} K={wl['cols']} N={wl['rows']})")
+        if world > 1:
+            desc += f", {world} independent replicas"
+    elif world > 1 and wl["shard"] == "replica":
+        desc += f", {world} independent {rows}-row blocks (one per GPU, no exchange)"
+    elif world > 1:
+        desc += f", row-sharded {rows} rows per GPU + all-gather of y"
+    if wl["argmax"]:
+        desc += ", argmax fused"
+    return {"workload": name, "description": desc, "type": t, "rows_total": rows_total, "rows_per_gpu": rows,
+            "cols": wl["cols"], "batch": batch_of(wl),
+            "parallelism": ("replicas" if wl["shard"] == "replica" else f"rowshard{world}") if world > 1 else "single"}
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi sampling of SM clock and throttle reasons during a region."""
@@ -164,11 +206,11 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        fd, self.path = tempfile.mkstemp(prefix="nedo_clocks_", suffix=".csv")
+        os.close(fd)
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -200,6 +242,10 @@ class ClockSampler:
                 for n, v in zip(names, parts[5:9]):
                     if v.lower() == "active":
                         reasons.add(n)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
@@ -210,19 +256,25 @@ class ClockSampler:
 CPU_BATCH_SAMPLE = 8
 
 
-def cpu_reference(type_, rows, cols, seed, nvec=1):
-    """(callable, kind, cores) running the reference CPU kernel: `nvec` matvecs over one matrix."""
+def checkers():
+    """(reference or None, oracle) from oracle/ -- the CPU baseline leg's checkers."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    w = B.gen_weight(type_, rows, cols, seed)
-    xs = [B.gen_x(cols, seed + k) for k in range(nvec)]
+    ref = None
     if O.Reference.available():
         ref = O.Reference()
-        cores = host_cores()
-        ref.set_threads(cores)
-        return (lambda: [ref.matvec(type_, rows, cols, w, x) for x in xs]), "reference", cores
-    orc = O.Oracle()
+        ref.set_threads(host_cores())
+    return ref, O.Oracle()
+
+
+def cpu_reference(type_, rows, cols, seed, nvec=1):
+    """(callable, kind, cores) running the reference CPU kernel: `nvec` matvecs over one matrix."""
+    ref, orc = checkers()
+    w = B.gen_weight(type_, rows, cols, seed)
+    xs = [B.gen_x(cols, seed + k) for k in range(nvec)]
+    if ref is not None:
+        return (lambda: [ref.matvec(type_, rows, cols, w, x) for x in xs]), "reference", host_cores()
     return (lambda: [orc.matvec(type_, rows, cols, w, x) for x in xs]), "port", 1
 
 
@@ -247,6 +299,38 @@ def cpu_baseline(wl, rows_total, budget_s=10.0):
             "sample": f"{n} x {what} ({sec * 1e3:.3f} ms each, {n * sec:.1f} s)"}
 
 
+def check_sample(sample):
+    """Checker of the CPU baseline leg: one GPU output against the reference on
+    the same bytes.  `sample` = list of (name, type, rows, cols, w bytes, x [k, cols],
+    y_gpu [k, rows], argmax index or None)."""
+    ref, orc = checkers()
+    worst, checked, ok = 0.0, [], True
+    argmax = None
+    for name, t, rows, cols, w, x, y, idx in sample:
+        for k in range(x.shape[0]):
+            yr = (ref.matvec(t, rows, cols, w, x[k]) if ref is not None else orc.matvec(t, rows, cols, w, x[k]))
+            absd = orc.abs_dot(t, rows, cols, w, x[k])
+            err = np.abs(y[k].astype(np.float64) - yr.astype(np.float64))
+            bound = TOL * absd
+            r = float(np.max(err / np.maximum(bound, 1e-300)))
+            worst = max(worst, r)
+            ok = ok and bool(np.all(err <= bound))
+            if idx is not None and k == 0:
+                top = np.sort(yr.astype(np.float64))[-2:]
+                ri = orc.argmax(yr)
+                argmax = {"gpu": int(idx), "reference": int(ri), "equal": int(idx) == int(ri),
+                          "top2_gap": float(top[1] - top[0]), "gap_over_bound": float((top[1] - top[0]) / max(
+                              2 * TOL * float(absd.max()), 1e-300))}
+                ok = ok and argmax["equal"]
+        checked.append(f"{name} ({x.shape[0]} vector{'s' if x.shape[0] > 1 else ''})")
+    out = {"ok": ok, "max_err_over_bound": round(worst, 5), "tolerance": f"{TOL} * sum|w*x| per output",
+           "checker": "reference (oracle/_ref)" if ref is not None else "oracle (C restatement)",
+           "checked": ", ".join(checked)}
+    if argmax is not None:
+        out["argmax"] = argmax
+    return out
+
+
 def run_reference_arm(args, wl, world, rank):
     if rank != 0:
         return
@@ -255,7 +339,7 @@ def run_reference_arm(args, wl, world, rank):
         line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks)",
-                "config": {"workload": args.workload, "batch": batch_of(wl)},
+                "config": workload_config(args.workload, wl, world),
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -265,98 +349,120 @@ def run_reference_arm(args, wl, world, rank):
     fn, kind, cores = cpu_reference(wl["type"], rows_total, wl["cols"], seed=7, nvec=nvec)
     for _ in range(args.warmup):
         fn()
+    # ~1 s soak (OpenMP thread pool and CPU clocks up), as the GPU arm soaks
+    # before its timed region; it also sizes a step to ~25 ms of CPU work
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 1.0:
+        fn()
+        n += 1
+    per_call = (time.perf_counter() - t0) / n
+    reps = max(1, int(round(0.025 / per_call)))
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        fn()
-    sec = (time.perf_counter() - t0) / args.steps
+        for _ in range(reps):
+            fn()
+    sec = (time.perf_counter() - t0) / (args.steps * reps)
     units, unit, scale = work_of(wl, rows_total, batch=nvec)
-    gbs = units / sec / scale
+    value = units / sec / scale
+    what = (f"{nvec} full {B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} matvec"
+            f"{'s (a sample of the batch, one per token)' if nvec > 1 else ''}")
     line = {
-        "metric": METRIC, "value": round(gbs, 4), "unit": unit, "impl": "reference", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 4), "higher_is_better": True,
-        "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded GGUF blocks)",
+        "metric": METRIC, "value": round(value, 4), "unit": unit, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3 * reps, 4),
+        "higher_is_better": True, "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded GGUF blocks)",
         "config": workload_config(args.workload, wl, world),
-        "cpu_baseline": {"value": round(gbs, 4), "unit": unit, "cores": cores, "kind": kind,
-                         "sample": f"each step {nvec} full {B.TYPE_NAMES[wl['type']]} {rows_total}x{wl['cols']} "
-                                   f"matvec{'s (a sample of the batch, one per token)' if nvec > 1 else ''}"},
-        "e2e": {"value": round(gbs, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": cores, "kind": kind,
+                         "sample": f"each step {reps} x {what} after a 1 s soak"},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def workload_config(name, wl, world):
-    rows, rows_total = shard_rows(wl, world)
-    t = B.TYPE_NAMES[wl["type"]]
-    desc = f"{t} matvec {rows_total}x{wl['cols']} batch {batch_of(wl)}"
-    if batch_of(wl) > 1:
-        desc = (f"{t} {wl['rows']}x{wl['cols']} weight x {batch_of(wl)} token vectors "
-                f"(prefill GEMM, M={batch_of(wl)} K={wl['cols']} N={wl['rows']})")
-        if world > 1:
-            desc += f", {world} independent replicas"
-    elif world > 1 and wl["shard"] == "replica":
-        desc += f", {world} independent {rows}-row blocks (one per GPU, no exchange)"
-    elif world > 1:
-        desc += f", row-sharded {rows} rows per GPU + all-gather of y"
-    if wl["argmax"]:
-        desc += ", argmax fused"
-    return {"workload": name, "description": desc, "type": t, "rows_total": rows_total, "rows_per_gpu": rows,
-            "cols": wl["cols"], "batch": batch_of(wl),
-            "parallelism": ("replicas" if wl["shard"] == "replica" else f"rowshard{world}") if world > 1 else "single"}
-
-
 # ------------------------------------------------------------------ GPU arm
-def make_weights(torch, type_, rows, cols, copies, seed, device):
-    """`copies` independent seeded weights [copies, rows*row_bytes] (uint8) on device."""
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    nb = cols // 32
-    if type_ == B.F16:
-        w = (torch.randn((copies, rows, cols), generator=g, device=device) * 0.02).half()
-        return w.view(torch.uint8).reshape(copies, -1)
-    bb = B.BLOCK_BYTES[type_]
-    blk = torch.empty((copies, rows, nb, bb), dtype=torch.uint8, device=device)
-    if type_ == B.Q8_0:
-        q = torch.randint(-127, 128, (copies, rows, nb, 32), generator=g, device=device, dtype=torch.int16)
-        blk[..., 2:] = q.to(torch.int8).view(torch.uint8)
-        d = (torch.randn((copies, rows, nb), generator=g, device=device).abs() * (0.02 / 127.0)).half()
-    else:
-        blk[..., 2:] = torch.randint(0, 256, (copies, rows, nb, 16), generator=g, device=device,
-                                     dtype=torch.int16).to(torch.uint8)
-        d = (torch.randn((copies, rows, nb), generator=g, device=device).abs() * (0.02 / 8.0)).half()
-    blk[..., 0:2] = d.contiguous().view(torch.uint8).reshape(copies, rows, nb, 2)
-    return blk.reshape(copies, -1)
+class Ctx:
+    """Per-process GPU state shared by the measurements."""
+
+    def __init__(self, args, world, rank, local_rank):
+        import torch
+        import torch.distributed as dist
+
+        import nedo_gpu
+
+        self.torch, self.dist = torch, dist
+        self.args, self.world, self.rank, self.local_rank = args, world, rank, local_rank
+        torch.cuda.set_device(local_rank)
+        self.device = torch.device("cuda", local_rank)
+        self.lib = nedo_gpu.load()
+        # Programmatic dependent launch: each matvec starts streaming its weight
+        # while the previous launch drains (x is read only after it completed).
+        self.lib.set_pdl(True)
+        self.stream = torch.cuda.Stream(device=self.device)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
+            return v
+        tt = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
+        self.dist.all_reduce(tt, op=self.dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    def timed_graph(self, graph, clocks=True):
+        """(ms of one replay, clocks): 1 s soak, then one replay between barriers + syncs."""
+        torch = self.torch
+        sampler = ClockSampler(self.local_rank) if clocks else None
+        if sampler:
+            sampler.start()
+        soak_end = time.perf_counter() + 1.0
+        while time.perf_counter() < soak_end:  # clocks under load before the timed region
+            graph.replay()
+            torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(self.stream):
+            ev0.record(self.stream)
+            graph.replay()
+            ev1.record(self.stream)
+        torch.cuda.synchronize()
+        self.barrier()
+        ms = self.max_over_ranks(ev0.elapsed_time(ev1))
+        return ms, (sampler.stop() if sampler else None)
 
 
-def run_gpu_arm(args, wl, world, rank, local_rank):
-    import torch
-    import torch.distributed as dist
+def launches_per_call(plan, nb):
+    """Kernels of this library one matvec_dev call launches."""
+    p = plan.get("path")
+    if p == 5:  # x -> fp16, the GEMM, and the split-K fold when K is split
+        return 3 if plan.get("slots", 1) > 1 else 2
+    if p == 3 and nb > 1:  # one streaming launch per vector
+        return nb
+    if p == 4 and nb > 1:  # int8 launches of 8, 4, 2 and 1 vectors
+        return nb // 8 + bin(nb % 8).count("1")
+    return 1
 
-    import nedo_gpu
-    from nedo_gpu.shard import FusedShardedMatvec, ShardedMatvec
 
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    lib = nedo_gpu.load()
-    # Programmatic dependent launch: each matvec starts streaming its weight
-    # while the previous launch drains (x is read only after it completed).
-    lib.set_pdl(True)
-    t, cols = wl["type"], wl["cols"]
-    rows, rows_total = shard_rows(wl, world)
-    rb = B.row_bytes(t, cols)
-    shard_bytes = rows * rb
-    copies = max(1, math.ceil(4 * L2_BYTES / shard_bytes))
-    w = make_weights(torch, t, rows, cols, copies, seed=1000 + rank, device=device)
-    gx = torch.Generator(device=device)
-    gx.manual_seed(7)
+def measure_matvec(ctx, name, steps, keep_sample=False):
+    """One matvec workload on this GPU alone (N=1 replica semantics): the value,
+    the roofline, clocks and (optionally) a sample for the checker."""
+    torch, lib = ctx.torch, ctx.lib
+    wl = WORKLOADS[name]
+    t, rows, cols = wl["type"], wl["rows"], wl["cols"]
     nb = batch_of(wl)
-    x = torch.randn((nb, cols) if nb > 1 else cols, generator=gx, device=device, dtype=torch.float32)
-    y = torch.empty((nb, rows) if nb > 1 else rows, dtype=torch.float32, device=device)
-    y_full = torch.empty(rows_total, dtype=torch.float32, device=device) if world > 1 and nb == 1 else y
-    idx = torch.zeros(1, dtype=torch.int64, device=device)
-    val = torch.zeros(1, dtype=torch.float32, device=device)
-    stream = torch.cuda.Stream(device=device)
+    rb = B.row_bytes(t, cols)
+    copies = max(1, math.ceil(4 * L2_BYTES / (rows * rb)))
+    w = B.gen_weight_torch(torch, t, rows, cols, copies, seed=1000 + ctx.rank, device=ctx.device)
+    gx = torch.Generator(device=ctx.device)
+    gx.manual_seed(7)
+    x = torch.randn((nb, cols) if nb > 1 else cols, generator=gx, device=ctx.device, dtype=torch.float32)
+    y = torch.empty((nb, rows) if nb > 1 else rows, dtype=torch.float32, device=ctx.device)
+    idx = torch.zeros(1, dtype=torch.int64, device=ctx.device)
+    val = torch.zeros(1, dtype=torch.float32, device=ctx.device)
     plan = lib.plan_info(t, rows, cols, nb)
+    lib.reserve(t, rows, cols, nb)
 
     def launch(k, s):
         wp = w[k % copies].data_ptr()
@@ -365,175 +471,72 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
         else:
             lib.matvec_dev(t, rows, cols, wp, x.data_ptr(), y.data_ptr(), nb, s)
 
-    # N > 1: this rank's rows, then every rank gets all of y -- fused into the
-    # int8 tensor-pipe kernel as NVLink peer stores where it takes the shape,
-    # else an NCCL all-gather (replica workloads run independently: no collective)
-    sm = fm = None
-    collective = None
-    if world > 1 and wl["shard"] != "replica":
-        if plan.get("path") == 4 and nb == 1:
-            fm = FusedShardedMatvec(lib, t, rows_total, cols, device)
-            collective = "fused: rows stored on every peer over NVLink by the matvec kernel + completion wait"
-        else:
-            sm = ShardedMatvec(t, rows_total, cols)
-            collective = "NCCL all-gather of the y slices"
-
-    def step(k):
-        if fm is not None:
-            fm.run(w[k % copies].data_ptr(), x.data_ptr(), torch.cuda.current_stream().cuda_stream)
-        elif sm is not None:
-            sm.run(lambda xv, yl: launch(k, stream.cuda_stream), x, y, y_full)
-        else:
-            launch(k, stream.cuda_stream)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        tt = torch.tensor([v], dtype=torch.float64, device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        return float(tt.item())
-
-    with torch.cuda.stream(stream):
-        for k in range(max(3, args.warmup)):
-            step(k)
+    with torch.cuda.stream(ctx.stream):
+        for k in range(max(3, ctx.args.warmup)):
+            launch(k, ctx.stream.cuda_stream)
     torch.cuda.synchronize()
-    lib.status(stream.cuda_stream)
-
-    # Kernel-only CUDA graph of K launches (the roofline's launch duration and, at
-    # N=1, the whole step).
+    lib.status(ctx.stream.cuda_stream)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for k in range(args.steps):
+    with torch.cuda.graph(graph, stream=ctx.stream):
+        for k in range(steps):
             launch(k, torch.cuda.current_stream().cuda_stream)
     graph.replay()
     torch.cuda.synchronize()
-    # N > 1: the whole step (matvec + all-gather) as one graph of K steps (K
-    # rounded to even: the fused path alternates two gathered buffers); every
-    # rank captures the same collectives in the same order
-    step_graph = None
-    if world > 1:
-        step_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(step_graph, stream=stream):
-            for k in range(args.steps + (args.steps & 1)):
-                step(k)
-        step_graph.replay()
-        torch.cuda.synchronize()
-        barrier()
-
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    soak_end = time.perf_counter() + 1.0
-    while time.perf_counter() < soak_end:  # clocks under load before the timed region
-        graph.replay()
-        torch.cuda.synchronize()
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        if world == 1:
-            graph.replay()
-        else:
-            step_graph.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    region_ms = max_over_ranks(ev0.elapsed_time(ev1))
-    if world > 1:
-        region_ms *= args.steps / (args.steps + (args.steps & 1))
-    clocks = sampler.stop()
-
-    # kernel-only timing (all ranks, for the roofline)
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        k0.record(stream)
-        graph.replay()
-        k1.record(stream)
-    torch.cuda.synchronize()
-    kernel_ms = max_over_ranks(k0.elapsed_time(k1)) / args.steps
-    lib.status(stream.cuda_stream)
+    ms, clocks = ctx.timed_graph(graph)
+    lib.status(ctx.stream.cuda_stream)
     del graph
-    del step_graph  # holds NCCL calls: released before the process group goes
-
-    units_total, unit, scale = work_of(wl, rows_total)  # whole job, all ranks
-    ms_per_step = region_ms / args.steps
-    value = units_total / (ms_per_step * 1e-3) / scale
-
-    # ---- end to end through the C ABI host entry point
-    e2e = e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream, fm)
-
+    ms_per_step = ms / steps
+    units, unit, scale = work_of(wl, rows)
+    value = units / (ms_per_step * 1e-3) / scale
     tensor = nb > 1
     peak, peak_kind = peaks(tensor)
-    per_launch, _, _ = work_of(wl, rows)
-    achieved = per_launch / (kernel_ms * 1e-3) / scale
-    traffic = NCU_TRAFFIC_BYTES.get(args.workload) if world == 1 else None
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-        "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None,
-        # block dots on the int8 tensor pipe (exact int32) for the IMMA plan; fp16
-        # operands with fp32 accumulation on tcgen05 for batches; fp32 FMA otherwise
-        "dtype": {4: "int8", 5: "f16"}.get(plan.get("path"), "f32"),
-        "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
-        "config": dict(workload_config(args.workload, wl, world),
-                       l2=f"{copies} rotating weight copies ({copies * shard_bytes / 2**20:.0f} MiB per GPU, "
-                          f"> 4x L2)", graph="K steps (matvec" + (" + NCCL all-gather" if world > 1 else "")
-                          + ") captured as one CUDA graph",
-                       pdl=True, plan=plan, **({"collective": collective} if collective else {})),
-        "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
-                     "launch_us": round(kernel_ms * 1e3, 3),
-                     ("flops_per_step" if tensor else "bytes_per_launch"): per_launch},
-        "e2e": e2e,
-        # one matvec kernel per step (argmax fused into it); batches: x -> fp16, then the GEMM
-        "gpu_launches": args.steps * (2 if plan.get("path") == 5 else 1),
-        "clocks": clocks,
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl, rows_total)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    out = {"value": round(value, 2), "unit": unit, "ms_per_step": round(ms_per_step, 6), "plan": plan,
+           "roofline": {"bound": "tensor" if tensor else "hbm", "achieved": round(value, 1), "peak": peak,
+                        "unit": unit, "frac": round(value / peak, 4), "traffic": NCU_TRAFFIC_BYTES.get(name),
+                        "peak_source": peak_kind, "launch_us": round(ms_per_step * 1e3, 3),
+                        ("flops_per_step" if tensor else "bytes_per_launch"): units},
+           "clocks": clocks, "copies": copies}
+    if keep_sample:
+        # one eager launch on copy 0 for the checker (a sample of 8 tokens of a batch)
+        with torch.cuda.stream(ctx.stream):
+            launch(0, ctx.stream.cuda_stream)
+        torch.cuda.synchronize()
+        kk = min(nb, CPU_BATCH_SAMPLE)
+        xs = x.reshape(nb, cols)[:kk].cpu().numpy()
+        ys = y.reshape(nb, rows)[:kk].cpu().numpy()
+        out["sample"] = [(name, t, rows, cols, w[0].cpu().numpy(), xs, ys,
+                          int(idx.item()) if wl["argmax"] else None)]
+    out["_state"] = (w, copies, x, y, launch, plan)
+    return out
 
 
-def run_sweep_arm(args, wl, world, rank, local_rank):
+def measure_sweep(ctx, name, steps_req, keep_sample=False):
     """Decode sweep: every matvec of one decoder step (plus the head) per step,
     all weights resident (918 MB: more than 4x L2, so each step reads HBM)."""
-    import torch
-    import torch.distributed as dist
-
-    import nedo_gpu
-
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    lib = nedo_gpu.load()
-    lib.set_pdl(True)
+    torch, lib = ctx.torch, ctx.lib
+    wl = WORKLOADS[name]
     nb = batch_of(wl)
     mats = sweep_matrices(wl)
-    ws = [make_weights(torch, t, r, c, 1, seed=2000 + 7 * i + rank, device=device)[0]
+    ws = [B.gen_weight_torch(torch, t, r, c, 1, seed=2000 + 7 * i + ctx.rank, device=ctx.device)[0]
           for i, (_, t, r, c) in enumerate(mats)]
     d, ff = wl["d"], wl["ff"]
-    g = torch.Generator(device=device)
+    g = torch.Generator(device=ctx.device)
     g.manual_seed(7)
-    xd = torch.randn((nb, d), generator=g, device=device)
-    xf = torch.randn((nb, ff), generator=g, device=device)
-    yd = torch.empty((nb, d), device=device)
-    yf = torch.empty((nb, ff), device=device)
-    logits = torch.empty((nb, wl["head"]), device=device)
-    idx = torch.zeros(1, dtype=torch.int64, device=device)
-    val = torch.zeros(1, dtype=torch.float32, device=device)
-    stream = torch.cuda.Stream(device=device)
+    xd = torch.randn((nb, d), generator=g, device=ctx.device)
+    xf = torch.randn((nb, ff), generator=g, device=ctx.device)
+    yd = torch.empty((nb, d), device=ctx.device)
+    yf = torch.empty((nb, ff), device=ctx.device)
+    logits = torch.empty((nb, wl["head"]), device=ctx.device)
+    idx = torch.zeros(1, dtype=torch.int64, device=ctx.device)
+    val = torch.zeros(1, dtype=torch.float32, device=ctx.device)
+    for _, t, r, c in mats:
+        lib.reserve(t, r, c, nb)
 
     def one(i, s):
-        name, t, r, c = mats[i]
+        nm, t, r, c = mats[i]
         x = xf if c == ff else xd
-        y = logits if name == "head" else (yf if r == ff else yd)
-        if name == "head" and wl["argmax"]:
+        y = logits if nm == "head" else (yf if r == ff else yd)
+        if nm == "head" and wl["argmax"]:
             lib.matvec_argmax_dev(t, r, c, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(), idx.data_ptr(),
                                   val.data_ptr(), s)
         else:
@@ -543,65 +546,41 @@ def run_sweep_arm(args, wl, world, rank, local_rank):
         for i in range(len(mats)):
             one(i, s)
 
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        tt = torch.tensor([v], dtype=torch.float64, device=device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        return float(tt.item())
-
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            step(stream.cuda_stream)
+    with torch.cuda.stream(ctx.stream):
+        for _ in range(max(3, ctx.args.warmup)):
+            step(ctx.stream.cuda_stream)
     torch.cuda.synchronize()
-    lib.status(stream.cuda_stream)
-    steps = max(1, min(args.steps, 50))  # about 1 ms per step
+    lib.status(ctx.stream.cuda_stream)
+    steps = max(1, min(steps_req, 50))  # about 1 ms per step
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
+    with torch.cuda.graph(graph, stream=ctx.stream):
         for _ in range(steps):
             step(torch.cuda.current_stream().cuda_stream)
     graph.replay()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    soak_end = time.perf_counter() + 1.0
-    while time.perf_counter() < soak_end:
-        graph.replay()
-        torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        graph.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms_per_step = max_over_ranks(ev0.elapsed_time(ev1)) / steps
-    clocks = sampler.stop()
+    ms, clocks = ctx.timed_graph(graph)
+    ms_per_step = ms / steps
     del graph
-    lib.status(stream.cuda_stream)
+    lib.status(ctx.stream.cuda_stream)
 
     # per matrix kind: the 24 layers' launches of one kind (or the head) as one graph
     kinds = {}
-    for i, (name, t, r, c) in enumerate(mats):
-        kinds.setdefault(name.rstrip("0123456789"), []).append(i)
+    for i, (nm, t, r, c) in enumerate(mats):
+        kinds.setdefault(nm.rstrip("0123456789"), []).append(i)
     per_kind = {}
     for kind, ids in kinds.items():
         kg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(kg, stream=stream):
+        with torch.cuda.graph(kg, stream=ctx.stream):
             for _ in range(3):
                 for i in ids:
                     one(i, torch.cuda.current_stream().cuda_stream)
         kg.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            a.record(stream)
+        with torch.cuda.stream(ctx.stream):
+            a.record(ctx.stream)
             kg.replay()
-            b.record(stream)
+            b.record(ctx.stream)
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / (3 * len(ids))
         _, t, r, c = mats[ids[0]]
@@ -610,115 +589,74 @@ def run_sweep_arm(args, wl, world, rank, local_rank):
                                                        "path": lib.plan_info(t, r, c, nb)["path"]}
         del kg
 
-    units_total = sweep_bytes(wl, nb) * world
-    value = units_total / (ms_per_step * 1e-3) / 1e9
+    units = sweep_bytes(wl, nb)
+    value = units / (ms_per_step * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    launches = sum(nb if (lib.plan_info(t, r, c, nb)["path"] in (3, 4) and nb > 1) else
-                   (2 if lib.plan_info(t, r, c, nb)["path"] == 5 else 1) for _, t, r, c in mats)
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
-        "config": {"workload": args.workload,
-                   "description": f"{wl['layers']}-layer d_model {d} decoder step: {len(mats) - 1} Q8_0 matvecs + "
-                                  f"F16 {wl['head']}x{d} head, {nb} token(s) per step",
-                   "batch": nb, "weight_bytes_per_step": sum(r * B.row_bytes(t, c) for _, t, r, c in mats),
-                   "parallelism": "replicas" if world > 1 else "single",
-                   "l2": "918 MB of weights, all resident: each step streams them from HBM (> 4x L2)",
-                   "graph": f"{steps} steps of {len(mats)} matvecs captured as one CUDA graph", "pdl": True,
-                   "per_matrix": per_kind},
-        "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(value / world / peak, 4), "traffic": None, "peak_source": peak_kind,
-                     "launch_us": round(ms_per_step * 1e3, 3), "bytes_per_step": sweep_bytes(wl, nb)},
-        "e2e": None,
-        "gpu_launches": steps * launches,
-        "clocks": clocks,
-    }
-    # end to end: pinned host x in, the step, pinned logits out
-    x_pin = torch.randn((nb, d)).pin_memory()
-    l_pin = torch.empty((nb, wl["head"])).pin_memory()
-    reps = 5
-    with torch.cuda.stream(stream):
-        xd.copy_(x_pin, non_blocking=True)
-        step(stream.cuda_stream)
-        l_pin.copy_(logits, non_blocking=True)
-    stream.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        with torch.cuda.stream(stream):
-            xd.copy_(x_pin, non_blocking=True)
-            step(stream.cuda_stream)
-            l_pin.copy_(logits, non_blocking=True)
-        stream.synchronize()
-    sec = max_over_ranks(time.perf_counter() - t0) / reps
-    line["e2e"] = {"value": round(units_total / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * nb * d,
-                   "d2h_bytes_per_step": 4 * nb * wl["head"], "path": "pinned H2D + 169 nedo_gpu_matvec_dev + D2H",
-                   "ms_per_step": round(sec * 1e3, 4)}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = sweep_cpu(wl, budget_s=10.0)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    launches = sum(launches_per_call(lib.plan_info(t, r, c, nb), nb) for _, t, r, c in mats)
+    out = {"value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms_per_step, 6), "steps": steps,
+           "per_matrix": per_kind, "launches_per_step": launches,
+           "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(value / peak, 4), "traffic": None, "peak_source": peak_kind,
+                        "launch_us": round(ms_per_step * 1e3, 3), "bytes_per_step": units},
+           "clocks": clocks}
+    if keep_sample:
+        with torch.cuda.stream(ctx.stream):
+            step(ctx.stream.cuda_stream)
+        torch.cuda.synchronize()
+        kk = min(nb, CPU_BATCH_SAMPLE)
+        sample = []
+        # one matrix of each kind, recomputed eagerly into its own output
+        for kind in ("q", "gate", "down", "head"):
+            i = kinds[kind][0]
+            nm, t, r, c = mats[i]
+            x = xf if c == ff else xd
+            yo = torch.empty((nb, r), device=ctx.device)
+            if nm == "head" and wl["argmax"]:
+                lib.matvec_argmax_dev(t, r, c, ws[i].data_ptr(), x.data_ptr(), yo.data_ptr(), idx.data_ptr(),
+                                      val.data_ptr(), ctx.stream.cuda_stream)
+            else:
+                lib.matvec_dev(t, r, c, ws[i].data_ptr(), x.data_ptr(), yo.data_ptr(), nb, ctx.stream.cuda_stream)
+            torch.cuda.synchronize()
+            sample.append((f"{nm} {B.TYPE_NAMES[t]} {r}x{c}", t, r, c, ws[i].cpu().numpy(), x[:kk].cpu().numpy(),
+                           yo[:kk].cpu().numpy(), int(idx.item()) if (nm == "head" and wl["argmax"]) else None))
+        out["sample"] = sample
+    out["_state"] = (mats, ws, xd, logits, step)
+    return out
 
 
-def sweep_cpu(wl, budget_s=10.0):
-    """The reference CPU kernels over one token of the sweep (all 169 matvecs)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-
-    mats = sweep_matrices(wl)
-    data = [(t, r, c, B.gen_weight(t, r, c, 3000 + i), B.gen_x(c, 3000 + i)) for i, (_, t, r, c) in enumerate(mats)]
-    if O.Reference.available():
-        ref, kind, cores = O.Reference(), "reference", host_cores()
-        ref.set_threads(cores)
-    else:
-        ref, kind, cores = O.Oracle(), "port", 1
-
-    def fn():
-        for t, r, c, w, x in data:
-            ref.matvec(t, r, c, w, x)
-
-    sec, n = time_cpu(fn, budget_s, 1000)
-    units = sweep_bytes(wl, 1)
-    return {"value": round(units / sec / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-            "sample": f"{n} x one token through all {len(mats)} matvecs ({sec * 1e3:.2f} ms each, {n * sec:.1f} s)"}
+def side_record(r):
+    keep = ("value", "unit", "ms_per_step", "roofline", "clocks", "parity", "per_matrix", "launches_per_step")
+    return {k: r[k] for k in keep if k in r}
 
 
-def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, rank, device, stream, fm=None):
+def e2e_matvec(ctx, wl, w, copies, rows, rows_total, fm=None):
+    torch, lib, dist = ctx.torch, ctx.lib, ctx.dist
+    world = ctx.world
+    stream = ctx.stream
     t, cols = wl["type"], wl["cols"]
     nb = batch_of(wl)
+    steps = ctx.args.steps
     if nb > 1:
-        # a prompt-sized batch end to end: pinned host x -> device, the batched
-        # matvec (x -> fp16 + tcgen05 GEMM), y -> pinned host, every step
-        x_pin = torch.from_numpy(np.random.default_rng(7).standard_normal((nb, cols), dtype=np.float32)).pin_memory()
-        y_pin = torch.empty((nb, rows), dtype=torch.float32).pin_memory()
-        xd = torch.empty((nb, cols), dtype=torch.float32, device=device)
-        yd = torch.empty((nb, rows), dtype=torch.float32, device=device)
-
-        def one(k):
-            with torch.cuda.stream(stream):
-                xd.copy_(x_pin, non_blocking=True)
-                lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), xd.data_ptr(), yd.data_ptr(), nb,
-                               stream.cuda_stream)
-                y_pin.copy_(yd, non_blocking=True)
-            stream.synchronize()
-
-        for k in range(3):
-            one(k)
-        if world > 1:
-            dist.barrier()
+        # a prompt-sized batch end to end through the host entry point
+        # (nedo_gpu_matvec_batch: host x in, host y out, resident weight)
+        x_host = np.random.default_rng(7).standard_normal((nb, cols), dtype=np.float32)
+        n_host = min(copies, 4)
+        hosts = [w[i].cpu().numpy() for i in range(n_host)]
+        for h in hosts:
+            lib.matvec_batch(t, rows, cols, h, x_host)
+        ctx.barrier()
         t0 = time.perf_counter()
-        for k in range(args.steps):
-            one(k)
-        sec = time.perf_counter() - t0
-        if world > 1:
-            tt = torch.tensor([sec], dtype=torch.float64, device=device)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            sec = float(tt.item())
-        sec /= args.steps
+        reps = max(1, min(steps, 50))
+        for k in range(reps):
+            y_host = lib.matvec_batch(t, rows, cols, hosts[k % n_host], x_host)
+        sec = ctx.max_over_ranks(time.perf_counter() - t0) / reps
+        assert y_host.shape == (nb, rows)
+        for h in hosts:
+            lib.weight_evict(h)
         units, unit, scale = work_of(wl, rows_total)
         return {"value": round(units / sec / scale, 2), "unit": unit, "h2d_bytes_per_step": 4 * nb * cols,
-                "d2h_bytes_per_step": 4 * nb * rows,
-                "path": "pinned H2D + nedo_gpu_matvec_dev(batch) + D2H", "ms_per_step": round(sec * 1e3, 4)}
+                "d2h_bytes_per_step": 4 * nb * rows, "path": "nedo_gpu_matvec_batch (host pointers, resident weight)",
+                "ms_per_step": round(sec * 1e3, 4)}
     x_host = np.random.default_rng(7).standard_normal(cols, dtype=np.float32)
     if world == 1 or wl["shard"] == "replica":
         # the host entry point (x and y in host memory) on every rank's own block
@@ -726,17 +664,11 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
         hosts = [w[i].cpu().numpy() for i in range(n_host)]
         for h in hosts:  # residency: first call uploads
             lib.matvec(t, rows, cols, h, x_host)
-        if world > 1:
-            dist.barrier()
+        ctx.barrier()
         t0 = time.perf_counter()
-        for k in range(args.steps):
+        for k in range(steps):
             y_host = lib.matvec(t, rows, cols, hosts[k % n_host], x_host)
-        sec = time.perf_counter() - t0
-        if world > 1:
-            tt = torch.tensor([sec], dtype=torch.float64, device=device)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            sec = float(tt.item())
-        sec /= args.steps
+        sec = ctx.max_over_ranks(time.perf_counter() - t0) / steps
         assert y_host.shape == (rows,)
         for h in hosts:
             lib.weight_evict(h)
@@ -744,12 +676,12 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
         return {"value": round(bytes_total / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * cols,
                 "d2h_bytes_per_step": 4 * rows, "path": "nedo_gpu_matvec (host pointers, resident weight)",
                 "ms_per_step": round(sec * 1e3, 4)}
-    # N > 1: pinned host x -> device, shard matvec, NCCL all-gather, full y -> host
+    # N > 1: pinned host x -> device, shard matvec, all-gather, full y -> host
     x_pin = torch.from_numpy(x_host).pin_memory()
     y_pin = torch.empty(rows_total, dtype=torch.float32).pin_memory()
-    xd = torch.empty(cols, dtype=torch.float32, device=device)
-    y = torch.empty(rows, dtype=torch.float32, device=device)
-    y_full = torch.empty(rows_total, dtype=torch.float32, device=device)
+    xd = torch.empty(cols, dtype=torch.float32, device=ctx.device)
+    y = torch.empty(rows, dtype=torch.float32, device=ctx.device)
+    y_full = torch.empty(rows_total, dtype=torch.float32, device=ctx.device)
 
     from nedo_gpu.shard import ShardedMatvec
 
@@ -770,18 +702,241 @@ def e2e_measure(args, lib, torch, dist, wl, w, copies, rows, rows_total, world, 
         one(k)
     dist.barrier()
     t0 = time.perf_counter()
-    for k in range(args.steps):
+    for k in range(steps):
         one(k)
-    sec = time.perf_counter() - t0
-    tt = torch.tensor([sec], dtype=torch.float64, device=device)
-    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    sec = float(tt.item()) / args.steps
+    sec = ctx.max_over_ranks(time.perf_counter() - t0) / steps
     bytes_total = algorithmic_bytes(t, rows_total, cols)
     return {"value": round(bytes_total / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * cols,
             "d2h_bytes_per_step": 4 * rows_total,
             "path": "pinned H2D + " + ("nedo_gpu_matvec_allgather_dev + wait" if fm is not None else
                                        "nedo_gpu_matvec_dev + NCCL all-gather") + " + D2H",
             "ms_per_step": round(sec * 1e3, 4)}
+
+
+def e2e_sweep(ctx, wl, state):
+    torch = ctx.torch
+    mats, ws, xd, logits, step = state
+    nb = batch_of(wl)
+    d = wl["d"]
+    x_pin = torch.randn((nb, d)).pin_memory()
+    l_pin = torch.empty((nb, wl["head"])).pin_memory()
+    reps = 5
+
+    def once():
+        with torch.cuda.stream(ctx.stream):
+            xd.copy_(x_pin, non_blocking=True)
+            step(ctx.stream.cuda_stream)
+            l_pin.copy_(logits, non_blocking=True)
+        ctx.stream.synchronize()
+
+    once()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        once()
+    sec = ctx.max_over_ranks(time.perf_counter() - t0) / reps
+    units = sweep_bytes(wl, nb) * ctx.world
+    return {"value": round(units / sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * nb * d,
+            "d2h_bytes_per_step": 4 * nb * wl["head"], "path": "pinned H2D + 169 nedo_gpu_matvec_dev + D2H",
+            "ms_per_step": round(sec * 1e3, 4)}
+
+
+def measure_sharded(ctx, name, steps):
+    """The row-sharded matvec at N = world ranks (strong scaling): matvec + the
+    fused all-gather (NCCL where that kernel does not take the shape).  Returns
+    the whole-job value and the per-step time split into the matvec alone and
+    the gather (the step minus the matvec, max over ranks)."""
+    torch, lib = ctx.torch, ctx.lib
+    from nedo_gpu.shard import FusedShardedMatvec, ShardedMatvec
+
+    wl = WORKLOADS[name]
+    t, cols = wl["type"], wl["cols"]
+    rows, rows_total = shard_rows(wl, ctx.world)
+    rb = B.row_bytes(t, cols)
+    copies = max(1, math.ceil(4 * L2_BYTES / (rows * rb)))
+    w = B.gen_weight_torch(torch, t, rows, cols, copies, seed=1000 + ctx.rank, device=ctx.device)
+    gx = torch.Generator(device=ctx.device)
+    gx.manual_seed(7)
+    x = torch.randn(cols, generator=gx, device=ctx.device, dtype=torch.float32)
+    y = torch.empty(rows, dtype=torch.float32, device=ctx.device)
+    y_full = torch.empty(rows_total, dtype=torch.float32, device=ctx.device)
+    plan = lib.plan_info(t, rows, cols, 1)
+    fm = sm = None
+    if plan.get("path") == 4:
+        fm = FusedShardedMatvec(lib, t, rows_total, cols, ctx.device)
+        collective = "fused: rows stored on every peer over NVLink by the matvec kernel + completion wait"
+    else:
+        sm = ShardedMatvec(t, rows_total, cols)
+        collective = "NCCL all-gather of the y slices"
+
+    def local(k, s):
+        lib.matvec_dev(t, rows, cols, w[k % copies].data_ptr(), x.data_ptr(), y.data_ptr(), 1, s)
+
+    def step(k):
+        if fm is not None:
+            fm.run(w[k % copies].data_ptr(), x.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        else:
+            sm.run(lambda xv, yl: local(k, torch.cuda.current_stream().cuda_stream), x, y, y_full)
+
+    with torch.cuda.stream(ctx.stream):
+        for k in range(4):
+            step(k)
+    torch.cuda.synchronize()
+    lib.status(ctx.stream.cuda_stream)
+    n = steps + (steps & 1)  # even: the fused path alternates two gathered buffers
+    g_local = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_local, stream=ctx.stream):
+        for k in range(n):
+            local(k, torch.cuda.current_stream().cuda_stream)
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=ctx.stream):
+        for k in range(n):
+            step(k)
+    g_local.replay()
+    g_step.replay()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ms_step, clocks = ctx.timed_graph(g_step)
+    ms_local, _ = ctx.timed_graph(g_local, clocks=False)
+    lib.status(ctx.stream.cuda_stream)
+    del g_step, g_local  # the step graph may hold NCCL calls: released before the process group
+    per = ms_step / n
+    units = algorithmic_bytes(t, rows_total, cols)
+    value = units / (per * 1e-3) / 1e9
+    return {"workload": name, "value": round(value, 2), "unit": "GB/s", "scaling": "strong",
+            "ms_per_step": round(per, 6), "matvec_ms": round(ms_local / n, 6),
+            "gather_ms": round(max(per - ms_local / n, 0.0), 6), "collective": collective,
+            "rows_per_gpu": rows, "n_gpus": ctx.world, "clocks": clocks,
+            "_state": (w, copies, fm)}
+
+
+def run_gpu_arm(args, wl, world, rank, local_rank):
+    ctx = Ctx(args, world, rank, local_rank)
+    torch = ctx.torch
+    name = args.workload
+    check = rank == 0 and world == 1 and not args.no_cpu_baseline
+    setup = {}
+    if wl.get("kind") == "sweep":
+        r = measure_sweep(ctx, name, args.steps, keep_sample=check)
+        e2e = e2e_sweep(ctx, wl, r["_state"])
+        value_total = r["value"] * world
+        line = {"metric": METRIC, "value": round(value_total, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": r["steps"], "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+f32",
+                "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
+                "config": workload_config(name, wl, world),
+                "setup": {"l2": "918 MB of weights, all resident: each step streams them from HBM (> 4x L2)",
+                          "graph": f"{r['steps']} steps of {len(sweep_matrices(wl))} matvecs captured as one CUDA graph",
+                          "pdl": True, "per_matrix": r["per_matrix"]},
+                "roofline": r["roofline"], "e2e": e2e, "gpu_launches": r["steps"] * r["launches_per_step"],
+                "clocks": r["clocks"]}
+        if check:
+            line["cpu_baseline"] = sweep_cpu(wl, budget_s=10.0)
+            line["parity"] = check_sample(r["sample"])
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
+
+    t, cols = wl["type"], wl["cols"]
+    rows, rows_total = shard_rows(wl, world)
+    nb = batch_of(wl)
+    if world == 1 or wl["shard"] == "replica":
+        r = measure_matvec(ctx, name, args.steps, keep_sample=check)
+        w, copies, x, y, launch, plan = r["_state"]
+        value_total = r["value"] * world if world > 1 else r["value"]
+        ms_per_step = r["ms_per_step"]
+        clocks = r["clocks"]
+        roofline = r["roofline"]
+        fm = None
+        collective = None
+        if world > 1:
+            # replicas: the max-over-ranks time of every rank's own block
+            value_total = work_of(wl, rows_total)[0] / (ms_per_step * 1e-3) / work_of(wl, rows_total)[2]
+    else:
+        r = measure_sharded(ctx, name, args.steps)
+        w, copies, fm = r["_state"]
+        plan = ctx.lib.plan_info(t, rows, cols, 1)
+        value_total = r["value"]
+        ms_per_step = r["ms_per_step"]
+        clocks = r["clocks"]
+        per_launch, unit, scale = work_of(wl, rows)
+        achieved = per_launch / (r["matvec_ms"] * 1e-3) / scale
+        peak, peak_kind = peaks()
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": unit,
+                    "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_kind,
+                    "launch_us": round(r["matvec_ms"] * 1e3, 3), "bytes_per_launch": per_launch}
+        collective = r["collective"]
+        setup["gather_ms"] = r["gather_ms"]
+        setup["matvec_ms"] = r["matvec_ms"]
+    setup.update({"l2": f"{copies} rotating weight copies ({copies * rows * B.row_bytes(t, cols) / 2**20:.0f} MiB "
+                        f"per GPU, > 4x L2)",
+                  "graph": "K steps (matvec" + (" + all-gather" if collective else "") +
+                           ") captured as one CUDA graph",
+                  "pdl": True, "plan": plan})
+    if collective:
+        setup["collective"] = collective
+    e2e = e2e_matvec(ctx, wl, w, copies, rows, rows_total, fm)
+    path = plan.get("path")
+    line = {
+        "metric": METRIC, "value": round(value_total, 2), "unit": roofline["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if wl["shard"] == "strong" else "weak", "vs_baseline": None,
+        # block dots on the int8 tensor pipe (exact int32) for the int8 plan; fp16
+        # operands with fp32 accumulation on tcgen05 for batches; fp32 FMA otherwise
+        "dtype": {4: "int8", 5: "f16"}.get(path, "f32"),
+        "data": "synthetic (seeded GGUF blocks, torch.Generator on device)",
+        "config": workload_config(name, wl, world), "setup": setup,
+        "roofline": roofline, "e2e": e2e,
+        # one matvec kernel per step (argmax fused into it); batches: x -> fp16, the GEMM (+ split-K fold)
+        "gpu_launches": args.steps * launches_per_call(plan, nb),
+        "clocks": clocks,
+    }
+    if check:
+        line["cpu_baseline"] = cpu_baseline(wl, rows_total)
+        line["parity"] = check_sample(r["sample"])
+    del r
+    if world == 1 and not args.no_side:
+        # every other configuration of the path, measured the same way in this run
+        side = {}
+        for other in SIDE_WORKLOADS:
+            if other == name:
+                continue
+            torch.cuda.empty_cache()
+            ow = WORKLOADS[other]
+            rr = (measure_sweep(ctx, other, 20, keep_sample=check) if ow.get("kind") == "sweep" else
+                  measure_matvec(ctx, other, 20 if batch_of(ow) == 1 else 10, keep_sample=check))
+            if check:
+                rr["parity"] = check_sample(rr.pop("sample"))
+            side[other] = side_record(rr)
+            del rr
+        line["workloads"] = side
+    elif world > 1 and name != "q4_0_32768x32768" and not args.no_side:
+        # the collective of the path: row-sharded Q4_0 32768x32768 at this N
+        torch.cuda.empty_cache()
+        rs = measure_sharded(ctx, "q4_0_32768x32768", 20)
+        rs.pop("_state")
+        line["sharded"] = rs
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def sweep_cpu(wl, budget_s=10.0):
+    """The reference CPU kernels over one token of the sweep (all 169 matvecs)."""
+    ref, orc = checkers()
+    mats = sweep_matrices(wl)
+    data = [(t, r, c, B.gen_weight(t, r, c, 3000 + i), B.gen_x(c, 3000 + i)) for i, (_, t, r, c) in enumerate(mats)]
+    if ref is not None:
+        kind, cores = "reference", host_cores()
+    else:
+        ref, kind, cores = orc, "port", 1
+
+    def fn():
+        for t, r, c, w, x in data:
+            ref.matvec(t, r, c, w, x)
+
+    sec, n = time_cpu(fn, budget_s, 1000)
+    units = sweep_bytes(wl, 1)
+    return {"value": round(units / sec / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"{n} x one token through all {len(mats)} matvecs ({sec * 1e3:.2f} ms each, {n * sec:.1f} s)"}
 
 
 def main():
@@ -791,7 +946,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="q4_0_11008x4096", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (and its checker)")
+    ap.add_argument("--no-side", action="store_true", help="measure only --workload (no `workloads` / `sharded`)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = env_int("WORLD_SIZE", 1)
@@ -816,10 +972,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if wl.get("kind") == "sweep":
-            run_sweep_arm(args, wl, world, rank, local_rank)
-        else:
-            run_gpu_arm(args, wl, world, rank, local_rank)
+        run_gpu_arm(args, wl, world, rank, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -72,18 +72,44 @@ NEDO_GPU_API int nedo_gpu_version(void);
  * weights are immutable).  Returns the previous setting. */
 NEDO_GPU_API int nedo_gpu_set_pdl(int enable);
 
+/* Batched calls on the exact kernels only (process-wide, off by default).
+ * By default a batch of 16 or more Q8_0/Q4_0 vectors (4 or more for F16) with
+ * rows of at least 1024 elements runs one tcgen05 GEMM on fp16 operands: x
+ * and d*q are each rounded to fp16 once (relative error <= 2^-11 per
+ * factor), products and sums are fp32.  Its worst-case error is therefore
+ * about 2^-10 * sum_i |w_i x_i| per output, ten times the reference
+ * tolerance of 1e-4 * sum_i |w_i x_i|, reached only when the rounding errors
+ * of a row share one sign (e.g. a constant positive x against same-sign
+ * weights); on independent inputs they cancel and the results stay within
+ * the tolerance (tested at every benchmark shape).  When enabled, batches run
+ * the int8 tensor-pipe kernel (exact integer block dots, x carried with 28
+ * significant bits) or, for F16, one streaming pass per vector: within the
+ * tolerance by bound, at the cost of one weight pass per 8 (int8) or 1 (F16)
+ * vectors.  Returns the previous setting.  No reference counterpart. */
+NEDO_GPU_API int nedo_gpu_set_exact_batches(int enable);
+
 /* Message of the last failing call on this thread ("" if none). */
 NEDO_GPU_API const char* nedo_gpu_last_error(void);
+
+/* Bound of every spin-wait of the kernels on the current device, in
+ * nanoseconds (0 restores the default of 2 s).  A wait that runs out makes
+ * its kernel wind down and record the failure, which the next
+ * nedo_gpu_status / host call reports as NEDO_GPU_ERR_DEVICE; the device stays
+ * usable.  No reference counterpart (the reference has no device waits). */
+NEDO_GPU_API int nedo_gpu_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------
  * Host-pointer entry points: drop-in semantics of the reference.
  *
  * Synchronous: the result is in y_host/out_host on return, like the CPU
- * kernel.  The weight bytes are uploaded to the device on first use and kept
- * resident, keyed by (w_host, w_bytes) -- the reference passes spans into a
- * GGUF mmap that stay valid and unchanged for the model's lifetime
- * (src/gguf.cpp:139).  A caller that rewrites a weight buffer in place must
- * call nedo_gpu_weight_evict() first.  Calls are serialised per device.
+ * kernel.  The weight bytes are uploaded to the device on first use (through
+ * pinned bounce buffers) and kept resident, keyed by (w_host, w_bytes) and a
+ * content fingerprint (first and last 4 KB plus 64 samples, checked on every
+ * call) -- the reference passes spans into a GGUF mmap that stay valid and
+ * unchanged for the model's lifetime (src/gguf.cpp:139).  A buffer freed and
+ * reused at the same address with other bytes is uploaded again.  A caller
+ * that rewrites a weight buffer in place where the fingerprint does not look
+ * must call nedo_gpu_weight_evict() first.  Calls are serialised per device.
  * ------------------------------------------------------------------------- */
 
 /* Replaces nedo::kernels::matvec (src/kernels.cpp:162-169):
@@ -94,6 +120,15 @@ NEDO_GPU_API const char* nedo_gpu_last_error(void);
  * w_bytes must be at least rows * row_bytes. */
 NEDO_GPU_API int nedo_gpu_matvec(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
                     const float* x_host, float* y_host);
+
+/* `batch` calls of nedo_gpu_matvec over one weight in one call:
+ * y_host[b][r] = dot(row r, x_host[b]), b < batch (x_host [batch][cols],
+ * y_host [batch][rows]).  Replaces the reference's prompt loop, one matvec per
+ * token for every weight (src/model.cpp:262-266, the forward lambda at
+ * :212-260), with one pass over the weight; the kernel choice is that of
+ * nedo_gpu_matvec_dev with the same batch.  Errors as nedo_gpu_matvec. */
+NEDO_GPU_API int nedo_gpu_matvec_batch(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host,
+                                       uint64_t w_bytes, const float* x_host, float* y_host, uint32_t batch);
 
 /* Replaces nedo::kernels::embedding_row (src/kernels.cpp:170-176): writes the
  * dequantised row `row` (cols floats) to out_host, bit-identical to the
@@ -106,7 +141,9 @@ NEDO_GPU_API int nedo_gpu_embedding_row(uint32_t type, uint64_t rows, uint64_t c
 NEDO_GPU_API int nedo_gpu_weight_upload(const void* w_host, uint64_t w_bytes, const void** w_dev_out);
 /* Drop the resident copy of w_host (no-op if absent). */
 NEDO_GPU_API int nedo_gpu_weight_evict(const void* w_host);
-/* Drop every resident weight on every device this library touched. */
+/* Drop every resident weight on every device this library touched, and free
+ * the batched-call buffers that larger calls replaced (a CUDA graph captured
+ * with one of those is invalid afterwards). */
 NEDO_GPU_API int nedo_gpu_cache_clear(void);
 
 /* ---------------------------------------------------------------------------
@@ -119,12 +156,23 @@ NEDO_GPU_API int nedo_gpu_cache_clear(void);
  * calls over the same weight, which is how the reference processes a prompt
  * (src/model.cpp:262-266).  For rows of at least 1024 elements, from 16
  * vectors on (4 for F16 weights) the batch runs as one tensor-core GEMM with x
- * and the dequantised weight rounded to fp16 (fp32 accumulation); the first
- * such call on a device allocates an fp16 copy of x and, for few row tiles, a
- * split-K workspace.  Such calls on one device share these buffers:
+ * and the dequantised weight rounded to fp16 (fp32 accumulation).  Those
+ * calls use two per-device buffers (an fp16 copy of x and, for few row tiles,
+ * a split-K workspace), allocated by the first call that needs them and grown
+ * by a larger one.  A grown-out buffer stays allocated until
+ * nedo_gpu_cache_clear, so a CUDA graph captured earlier keeps working.  To
+ * capture such a call in a graph, size the buffers first, outside capture,
+ * with nedo_gpu_reserve (or one eager call of the largest shape): a call that
+ * has to allocate cannot be captured.  Calls on one device share the buffers:
  * serialise calls that may overlap (other streams, other threads). */
 NEDO_GPU_API int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
                         float* y_dev, uint32_t batch, void* stream);
+
+/* Size the per-device buffers of a batched nedo_gpu_matvec_dev call of this
+ * shape (no-op for shapes that need none), so that the call itself allocates
+ * nothing and can be captured in a CUDA graph.  Call outside stream capture.
+ * No reference counterpart. */
+NEDO_GPU_API int nedo_gpu_reserve(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch);
 
 /* matvec followed by the greedy pick of the LM head (std::max_element over
  * the logits, src/model.cpp:36: first index of the maximum), fused into the
@@ -135,7 +183,10 @@ NEDO_GPU_API int nedo_gpu_matvec_dev(uint32_t type, uint64_t rows, uint64_t cols
 NEDO_GPU_API int nedo_gpu_matvec_argmax_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
                                float* y_dev, int64_t* index_dev, float* value_dev, void* stream);
 
-/* argmax of an fp32 vector in device memory (first index of the maximum). */
+/* argmax of an fp32 vector in device memory (first index of the maximum).
+ * NaN behaves as in std::max_element: a NaN never wins, except that a NaN at
+ * index 0 makes the result 0 (every comparison with it is false); this holds
+ * for every argmax entry point. */
 NEDO_GPU_API int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev, void* stream);
 
 /* nedo_gpu_argmax_dev without any allocation: the same kernel and result,
@@ -163,11 +214,14 @@ NEDO_GPU_API int nedo_gpu_matvec_allgather_dev(uint32_t type, uint64_t rows, uin
                                   const float* x_dev, float* y_dev, const uint64_t* peer_y,
                                   const uint64_t* peer_signal, uint32_t npeers, uint64_t row_offset, void* stream);
 
-/* Wait on `stream` (one GPU thread, bounded to 2 s; a timeout sets the status
- * word read by nedo_gpu_status) until *signal_dev has advanced by `increment`
- * (peers x CTAs of their launches) past *expected_dev, then advance
- * *expected_dev.  Both words start at zero; the caller keeps them per
- * receiving buffer. */
+/* Wait on `stream` (one GPU thread, bounded by nedo_gpu_set_wait_limit_ns, 2 s
+ * by default; a timeout sets the status word read by nedo_gpu_status) until
+ * *signal_dev has advanced by `increment` (peers x CTAs of their launches)
+ * past *expected_dev, then advance *expected_dev by `increment` -- also after
+ * a timeout, so that signals of a late step are never counted for the next
+ * one.  After NEDO_GPU_ERR_DEVICE the gathered rows of that step are invalid;
+ * later steps are correct once the late peer has caught up.  Both words start
+ * at zero; the caller keeps them per receiving buffer. */
 NEDO_GPU_API int nedo_gpu_allgather_wait_dev(uint32_t* signal_dev, uint32_t* expected_dev, uint32_t increment,
                                 void* stream);
 
@@ -184,8 +238,9 @@ NEDO_GPU_API int nedo_gpu_status(void* stream);
  * 2 generic, 3 batched streaming (one launch per vector), 4 int8 tensor-pipe
  * matvec, 5 tcgen05 GEMM over the batch), out[1] grid,
  * out[2] threads, out[3] dynamic shared bytes, out[4] rows per tile,
- * out[5] ring slots, out[6] slot bytes, out[7] warps per CTA (compute warps for
- * path 4).  n = capacity of out (>= 8). */
+ * out[5] ring slots (path 5: K splits per tile, > 1 adding a fold kernel),
+ * out[6] slot bytes, out[7] warps per CTA (compute warps for path 4).
+ * n = capacity of out (>= 8). */
 NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
 
 #ifdef __cplusplus

@@ -1,6 +1,6 @@
 // Declaration-compatible subset of nedo.cpp's include/nedo/kernels.hpp: the two
-// hot-path entry points (kernels.hpp:20-21) and the fp16 helpers the kernel
-// tests use (kernels.hpp:9-10).
+// hot-path entry points (kernels.hpp:20-21), the fp16 helpers the kernel
+// tests use (kernels.hpp:9-10), and the drop-in's added batched matvec.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -13,4 +13,7 @@ float fp16_to_fp32(uint16_t h) noexcept;
 uint16_t fp32_to_fp16(float f) noexcept;
 void matvec(const TensorInfo& t, std::span<const std::byte> bytes, const float* x, float* y);
 void embedding_row(const TensorInfo& t, std::span<const std::byte> bytes, uint32_t row, float* out);
+// Added by the B200 drop-in (no reference counterpart): `batch` matvecs over one
+// weight, x [batch][cols] -> y [batch][rows].
+void matvec_batch(const TensorInfo& t, std::span<const std::byte> bytes, const float* x, float* y, uint32_t batch);
 }  // namespace nedo::kernels

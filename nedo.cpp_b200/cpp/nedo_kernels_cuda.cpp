@@ -19,6 +19,15 @@
 //   * embedding_row: "bad embedding row" / "embedding type unsupported" (src/kernels.cpp:171,175)
 //   * synchronous: y[0..rows) is fully written when the call returns.
 // Added: a span shorter than rows*row_bytes throws instead of reading past it.
+//
+// Added entry point (no reference counterpart, declared in cpp/compat/nedo/kernels.hpp;
+// a maintainer adds the same line to the reference's include/nedo/kernels.hpp):
+//   void nedo::kernels::matvec_batch(const TensorInfo&, std::span<const std::byte>,
+//                                    const float* x, float* y, uint32_t batch);
+// `batch` matvecs over one weight, x [batch][cols] -> y [batch][rows], with the
+// same checks and messages as matvec.  It replaces the prompt loop of
+// src/model.cpp:262-266 (one forward per token, each weight read per token)
+// with one pass over each weight for the whole prompt.
 #include <cstddef>
 #include <cstdint>
 #include <span>
@@ -44,6 +53,17 @@ void matvec(const TensorInfo& t, std::span<const std::byte> b, const float* x, f
     if (!gpu_type(t.type)) throw std::runtime_error("matvec tensor type not supported");
     if (b.size() < rows * rowbytes) throw std::runtime_error("matvec: tensor bytes shorter than its shape: " + t.name);
     const int rc = nedo_gpu_matvec(static_cast<uint32_t>(t.type), rows, cols, b.data(), b.size(), x, y);
+    if (rc != NEDO_GPU_OK) raise_gpu(rc);
+}
+
+void matvec_batch(const TensorInfo& t, std::span<const std::byte> b, const float* x, float* y, uint32_t batch) {
+    if (t.shape.size() != 2) throw std::runtime_error("matvec requires rank-2 tensor: " + t.name);
+    const uint64_t cols = t.shape[0], rows = t.shape[1];
+    const uint64_t rowbytes = tensor_nbytes(t.type, cols);
+    if (rows == 0 || batch == 0) return;
+    if (!gpu_type(t.type)) throw std::runtime_error("matvec tensor type not supported");
+    if (b.size() < rows * rowbytes) throw std::runtime_error("matvec: tensor bytes shorter than its shape: " + t.name);
+    const int rc = nedo_gpu_matvec_batch(static_cast<uint32_t>(t.type), rows, cols, b.data(), b.size(), x, y, batch);
     if (rc != NEDO_GPU_OK) raise_gpu(rc);
 }
 

@@ -2,7 +2,8 @@
 // run through the drop-in nedo::kernels::matvec / embedding_row, i.e. on the GPU.
 // Same harness shape as the reference: plain int return codes, "ok" on success.
 // Added cases: an F16 row, a multi-row Q8_0 matrix large enough for the
-// streaming kernel, and the reference's error messages.
+// streaming kernel, the drop-in's batched matvec (512 token vectors), and the
+// reference's error messages.
 #include <cmath>
 #include <cstring>
 #include <iostream>
@@ -90,6 +91,44 @@ int test_q8_many_rows() {
     return 0;
 }
 
+int test_q8_batch() {
+    // The drop-in's added matvec_batch: 512 token vectors through one Q8_0
+    // 300 x 1024 weight (the batched tensor-core path), each checked against
+    // its serial dot product computed here in double.  Weights and x are small
+    // integers times powers of two, exact in every arithmetic the GPU may use.
+    const int rows = 300, cols = 1024, nb = cols / 32, batch = 512;
+    nedo::TensorInfo t{"q8batch", {uint64_t(cols), uint64_t(rows)}, nedo::TensorType::Q8_0};
+    std::vector<std::byte> w(size_t(rows) * nb * 34);
+    std::vector<float> deq(size_t(rows) * cols);
+    for (int r = 0; r < rows; ++r)
+        for (int b = 0; b < nb; ++b) {
+            std::byte* blk = w.data() + (size_t(r) * nb + b) * 34;
+            const float d = float(1 + (r + 3 * b) % 4) * 0.25f;
+            const uint16_t h = nedo::kernels::fp32_to_fp16(d);
+            std::memcpy(blk, &h, 2);
+            for (int i = 0; i < 32; ++i) {
+                const int8_t q = int8_t(((r * 29 + b * 13 + i * 7) % 255) - 127);
+                blk[2 + i] = std::byte(static_cast<unsigned char>(q));
+                deq[size_t(r) * cols + b * 32 + i] = d * float(q);
+            }
+        }
+    std::vector<float> x(size_t(batch) * cols), y(size_t(batch) * rows);
+    for (int k = 0; k < batch; ++k)
+        for (int i = 0; i < cols; ++i) x[size_t(k) * cols + i] = float((i * 7 + k * 3) % 11) - 5.f;
+    nedo::kernels::matvec_batch(t, w, x.data(), y.data(), batch);
+    for (int k = 0; k < batch; ++k)
+        for (int r = 0; r < rows; ++r) {
+            double e = 0.0, a = 0.0;
+            for (int i = 0; i < cols; ++i) {
+                const double p = double(deq[size_t(r) * cols + i]) * double(x[size_t(k) * cols + i]);
+                e += p;
+                a += std::abs(p);
+            }
+            if (std::abs(double(y[size_t(k) * rows + r]) - e) > 1e-4 * a) return 14;
+        }
+    return 0;
+}
+
 template <typename F>
 bool throws_with(F&& f, const std::string& msg) {
     try {
@@ -113,6 +152,10 @@ int test_errors() {
     if (!throws_with([&] { nedo::kernels::matvec(q4k, w, x, y); }, "tensor type not implemented: 12")) return 12;
     nedo::TensorInfo q8{"q8", {64, 2}, nedo::TensorType::Q8_0};
     if (!throws_with([&] { nedo::kernels::embedding_row(q8, w, 2, y); }, "bad embedding row")) return 13;
+    if (!throws_with([&] { nedo::kernels::matvec_batch(rank1, w, x, y, 2); }, "matvec requires rank-2 tensor: r1"))
+        return 15;
+    if (!throws_with([&] { nedo::kernels::matvec_batch(f32, w, x, y, 2); }, "matvec tensor type not supported"))
+        return 16;
     return 0;
 }
 }  // namespace
@@ -122,6 +165,7 @@ int main() {
     if (int rc = test_q4_matvec_and_embedding()) return rc;
     if (int rc = test_f16_matvec()) return rc;
     if (int rc = test_q8_many_rows()) return rc;
+    if (int rc = test_q8_batch()) return rc;
     if (int rc = test_errors()) return rc;
     std::cout << "ok\n";
     return 0;

@@ -7,8 +7,13 @@
 // rank's stream: it waits until its signal word has advanced by `increment`
 // (peers x CTAs per launch) past the expected value kept in device memory,
 // then advances that value, so the same launch works unchanged in a CUDA graph
-// replayed many times.  The wait is bounded (2 s); on timeout it records the
-// failure in DeviceStatus and returns.
+// replayed many times.  The wait is bounded (2 s by default, the device's
+// DeviceStatus::wait_limit_ns when set); on timeout it records the failure in
+// DeviceStatus and still advances the expected value by `increment`.  Every
+// step thus consumes exactly `increment` arrivals: signals of a step that
+// arrive after its wait gave up count toward that step, never toward the
+// next one, so a late peer cannot make the next step read stale rows.  The
+// gathered buffer of a step that reported NEDO_GPU_ERR_DEVICE is invalid.
 //
 // With programmatic dependent launch the wait kernel starts while this rank's
 // matvec is still running (its CTA fits beside the matvec's), so the peers'
@@ -30,11 +35,13 @@ __global__ void gather_wait_kernel(uint32_t* signal, uint32_t* expected, uint32_
     const uint32_t target = *expected + increment;  // wraps with the counter
     volatile uint32_t* sig = signal;
     const uint64_t t0 = global_timer_ns();
+    const uint64_t limit = wait_limit_ns(status);
     // counters wrap: "reached" is a non-negative signed distance
     while (static_cast<int32_t>(*sig - target) < 0) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit) {
             if (atomicOr(&status->flags, kErrWaitTimeout) == 0u) status->where = 40u;
             asm volatile("griddepcontrol.wait;" ::: "memory");
+            *expected = target;  // this step's arrivals stay this step's, late or not
             return;
         }
         __nanosleep(200);

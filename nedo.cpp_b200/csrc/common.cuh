@@ -21,12 +21,22 @@ enum : uint32_t {
 
 struct DeviceStatus {
     uint32_t flags;
-    uint32_t where;  // site id of the first failure (diagnostics only)
+    uint32_t where;          // site id of the first failure (diagnostics only)
+    uint64_t wait_limit_ns;  // bound of every spin-wait (set by the host; 0 = kWaitLimitNs)
 };
 
-// Upper bound of every spin-wait in these kernels.  Any wait that a correct
-// launch performs ends in microseconds; two seconds means something is wrong.
+// Default upper bound of every spin-wait in these kernels.  Any wait that a
+// correct launch performs ends in microseconds; two seconds means something is
+// wrong.  The host may lower it per device (DeviceStatus::wait_limit_ns).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// The bound a kernel applies: read only once a wait has already failed its
+// first try, so the load costs nothing on the fast path.
+__device__ __forceinline__ uint64_t wait_limit_ns(const DeviceStatus* st) {
+    if (st == nullptr) return kWaitLimitNs;
+    const uint64_t v = *reinterpret_cast<const volatile uint64_t*>(&st->wait_limit_ns);
+    return v != 0 ? v : kWaitLimitNs;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -77,9 +87,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, DeviceStatus* st, uint32_t site) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
+    const uint64_t limit = wait_limit_ns(st);
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit) {
             if (st != nullptr) {
                 if (atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
             }

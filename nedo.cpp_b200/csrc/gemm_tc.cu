@@ -517,7 +517,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __rest
 // ---- host side ----------------------------------------------------------
 template <uint32_t TYPE>
 cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
-                     uint32_t ldy, uint32_t ksplit, uint64_t split_stride, DeviceStatus* status, cudaStream_t stream) {
+                     uint32_t ldy, uint32_t ksplit, uint64_t split_stride, DeviceStatus* status, cudaStream_t stream,
+                     bool pdl) {
     EncodeTiled enc = encode_tiled_fn();
     if (enc == nullptr) return cudaErrorNotSupported;
     CUtensorMap mw, mx;
@@ -568,8 +569,9 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     a.ksplit = ksplit;
     a.split_stride = split_stride;
     a.status = status;
-    // programmatic dependent launch: the CTAs start (TMEM, barriers, the first
-    // weight chunks and their dequantisation) while the previous kernel finishes
+    // programmatic dependent launch (when `pdl`): the CTAs start (TMEM, barriers,
+    // the first weight chunks and their dequantisation) while the previous
+    // kernel finishes
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((rows + kRows - 1) / kRows, (tokens + kBN - 1) / kBN, ksplit);
     cfg.blockDim = dim3(kThreads);
@@ -579,7 +581,7 @@ cudaError_t launch_t(const void* w, const __half* xh, float* y, uint32_t rows, u
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TYPE>, mw, mx, a);
 }
 
@@ -675,9 +677,10 @@ __device__ __forceinline__ bool try_wait_cluster(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ bool wait_cluster_bounded(uint64_t* bar, uint32_t parity, DeviceStatus* st, uint32_t site) {
     if (try_wait_cluster(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
+    const uint64_t limit = wait_limit_ns(st);
     while (true) {
         if (try_wait_cluster(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit) {
             if (st != nullptr && atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
             return false;
         }
@@ -884,7 +887,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <uint32_t TYPE>
 cudaError_t launch_pair_t(const void* w, const __half* xh, float* y, uint32_t rows, uint32_t cols, uint32_t tokens,
-                          uint32_t ldy, DeviceStatus* status, cudaStream_t stream) {
+                          uint32_t ldy, DeviceStatus* status, cudaStream_t stream, bool pdl) {
     EncodeTiled enc = encode_tiled_fn();
     if (enc == nullptr) return cudaErrorNotSupported;
     CUtensorMap mw, mx;
@@ -934,7 +937,7 @@ cudaError_t launch_pair_t(const void* w, const __half* xh, float* y, uint32_t ro
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<TYPE>, mw, mx, a);
 }
 
@@ -988,7 +991,7 @@ uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_s
 }
 
 cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uint64_t tokens, uint64_t rows,
-                                 uint64_t ldy, int num_sms, cudaStream_t stream) {
+                                 uint64_t ldy, int num_sms, cudaStream_t stream, bool pdl) {
     const uint64_t n = tokens * rows;
     uint64_t blocks = (n + 255u) / 256u;
     if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
@@ -1001,17 +1004,17 @@ cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uin
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, ws, y, splits, static_cast<uint32_t>(tokens),
                               static_cast<uint32_t>(rows), ldy);
 }
 
-cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream) {
+cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream, bool pdl) {
     uint64_t blocks = (n / 4u + 255u) / 256u;
     if (blocks > static_cast<uint64_t>(num_sms) * 8u) blocks = static_cast<uint64_t>(num_sms) * 8u;
     if (blocks == 0) blocks = 1;
-    // programmatic dependent launch: scheduled while the previous kernel runs,
-    // the conversion itself starts after that kernel's completion
+    // programmatic dependent launch (when `pdl`): scheduled while the previous
+    // kernel runs, the conversion itself starts after that kernel's completion
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<uint32_t>(blocks));
     cfg.blockDim = dim3(256);
@@ -1020,27 +1023,30 @@ cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms,
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, x_to_f16_kernel, x, xh, n);
 }
 
 cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
-                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream, uint32_t ksplit,
-                           uint64_t split_stride) {
+                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream, bool pdl,
+                           uint32_t ksplit, uint64_t split_stride) {
     if (!gemm_tc_supported(type, rows, cols, tokens)) return cudaErrorInvalidValue;
     if (ksplit == 0 || ksplit > (cols + kRawK - 1) / kRawK || ksplit > 65535u) return cudaErrorInvalidValue;
     const uint32_t r = static_cast<uint32_t>(rows), c = static_cast<uint32_t>(cols), t = static_cast<uint32_t>(tokens);
     if (use_pair(type, tokens, ksplit)) {
-        if (type == kQ8_0) return launch_pair_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
-        return launch_pair_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream);
+        if (type == kQ8_0) return launch_pair_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream, pdl);
+        return launch_pair_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), status, stream, pdl);
     }
     switch (type) {
         case kQ8_0:
-            return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
+            return launch_t<kQ8_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream,
+                                    pdl);
         case kQ4_0:
-            return launch_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
+            return launch_t<kQ4_0>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream,
+                                    pdl);
         case kF16:
-            return launch_t<kF16>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream);
+            return launch_t<kF16>(w, xh, y, r, c, t, static_cast<uint32_t>(ldy), ksplit, split_stride, status, stream,
+                                    pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -6,7 +6,9 @@
 //   * dequant_rows_kernel: embedding_row (src/kernels.cpp:170-176): one fp32
 //     multiply d*q per element, so the result is bit-identical to the reference.
 //   * argmax kernels: first index of the maximum (std::max_element,
-//     src/model.cpp:36).
+//     src/model.cpp:36), with its NaN behaviour: NaNs never win, except that
+//     a NaN at index 0 is returned (max_element starts from element 0 and no
+//     comparison with NaN succeeds).
 #include <math.h>
 
 #include "common.cuh"
@@ -137,6 +139,13 @@ __global__ void argmax_kernel(const float* __restrict__ v, uint64_t n, ArgmaxScr
                     fv = cv[k];
                     fi = ci[k];
                 }
+            // std::max_element keeps element 0 when it is NaN (nothing compares
+            // greater than NaN); otherwise NaNs never win, as in better().
+            const float v0 = v[0];
+            if (v0 != v0) {
+                fv = v0;
+                fi = 0u;
+            }
             *s.out_index = static_cast<int64_t>(fi);
             if (s.out_value != nullptr) *s.out_value = fv;
             *s.counter = 0u;

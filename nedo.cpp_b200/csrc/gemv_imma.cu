@@ -113,9 +113,10 @@ __device__ __forceinline__ bool wait_issued(volatile uint32_t* issued, uint32_t 
                                             DeviceStatus* st, uint32_t site) {
     if (*issued == want) return true;
     const uint64_t t0 = global_timer_ns();
+    const uint64_t limit = wait_limit_ns(st);
     while (*issued != want) {
         if (*abort_flag != 0u) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > limit) {
             if (atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
             return false;
         }

@@ -455,6 +455,13 @@ __global__ void __launch_bounds__(512, 1) gemv_stream_kernel(const StreamArgs a)
     }
     warp_argmax(bv, bi);
     if (lane == 0) {
+        // std::max_element keeps element 0 when it is NaN (no value compares
+        // greater than NaN); otherwise NaNs never win, as in amax_better.
+        const float y0 = __ldcg(a.y);
+        if (y0 != y0) {
+            bv = y0;
+            bi = 0u;
+        }
         *a.amax.out_index = static_cast<int64_t>(bi);
         if (a.amax.out_value != nullptr) *a.amax.out_value = bv;
         *a.amax.counter = 0u;  // ready for the next launch

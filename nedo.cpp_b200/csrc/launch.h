@@ -127,11 +127,13 @@ cudaError_t launch_argmax(const float* v, uint64_t n, ArgmaxScratch* scratch, in
 // row pitch ldy.  Supported: F16 / Q8_0 / Q4_0, cols % 32 == 0, 16-byte rows.
 bool gemm_tc_supported(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens);
 uint32_t gemm_tc_ctas(uint64_t rows, uint64_t tokens);  // CTAs of one launch (128 rows x 256 tokens each)
-cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream);
+cudaError_t launch_x_to_f16(const float* x, __half* xh, uint64_t n, int num_sms, cudaStream_t stream, bool pdl);
 // ksplit > 1: each tile's K is shared by ksplit CTAs, split z writing its partial
 // sums to y + z * split_stride (a workspace, folded by launch_splitk_reduce).
+// `pdl`: programmatic dependent launch (weights streamed before the previous
+// kernel on the stream completes; x read after it), for all three launches.
 cudaError_t launch_gemm_tc(uint32_t type, const void* w, const __half* xh, float* y, uint64_t rows, uint64_t cols,
-                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream,
+                           uint64_t tokens, uint64_t ldy, DeviceStatus* status, cudaStream_t stream, bool pdl,
                            uint32_t ksplit = 1, uint64_t split_stride = 0);
 // CTAs along K per tile for a GEMM whose tiles would leave most SMs idle (1 otherwise).
 uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms);
@@ -141,7 +143,7 @@ uint32_t gemm_tc_splits(uint64_t rows, uint64_t cols, uint64_t tokens, int num_s
 uint32_t gemm_tc_launch_ctas(uint32_t type, uint64_t rows, uint64_t cols, uint64_t tokens, int num_sms);
 // y[t * ldy + r] = sum_z ws[(z * tokens + t) * rows + r], z in order (deterministic).
 cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uint64_t tokens, uint64_t rows,
-                                 uint64_t ldy, int num_sms, cudaStream_t stream);
+                                 uint64_t ldy, int num_sms, cudaStream_t stream, bool pdl);
 
 uint64_t row_bytes_of(uint32_t type, uint64_t cols);
 

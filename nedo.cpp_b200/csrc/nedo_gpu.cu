@@ -48,6 +48,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 struct Resident {
     void* dev = nullptr;
     uint64_t bytes = 0;
+    uint64_t fingerprint = 0;  // content_fingerprint() of the host bytes at upload
     cudaGraphExec_t call = nullptr;
     uint32_t type = 0;
     uint64_t rows = 0, cols = 0;
@@ -79,6 +80,12 @@ struct DeviceState {
     uint64_t xh_cap = 0;
     float* splitk_ws = nullptr;  // split-K partial sums of the tensor-core GEMM
     uint64_t splitk_cap = 0;
+    // Buffers a larger call replaced.  A CUDA graph captured earlier may still
+    // name them, so they are freed only by nedo_gpu_cache_clear.
+    std::vector<void*> retired;
+    uint8_t* upload_pin[2] = {nullptr, nullptr};  // pinned bounce buffers of weight uploads
+    cudaEvent_t upload_done[2] = {nullptr, nullptr};
+    uint64_t wait_limit_ns = 0;  // 0 = the kernels' default bound
     std::unordered_map<const void*, Resident> cache;
     std::mutex mu;
 };
@@ -86,6 +93,7 @@ struct DeviceState {
 std::mutex g_states_mu;
 std::vector<DeviceState*> g_states;
 std::atomic<int> g_pdl{0};
+std::atomic<int> g_exact_batches{0};
 
 int current_device(int* dev) {
     cudaError_t e = cudaGetDevice(dev);
@@ -163,6 +171,22 @@ int ensure_dev(T** p, uint64_t* cap, uint64_t need) {
     return 0;
 }
 
+// Like ensure_dev for buffers that device entry points hand to kernels a
+// caller may capture in a CUDA graph: a buffer that is outgrown is retired
+// (kept allocated until nedo_gpu_cache_clear) instead of freed, so a graph
+// captured with it stays valid.
+template <typename T>
+int ensure_dev_retiring(DeviceState* s, T** p, uint64_t* cap, uint64_t need) {
+    if (*cap >= need) return 0;
+    T* fresh = nullptr;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&fresh), need * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(batched-call buffer)");
+    if (*p) s->retired.push_back(*p);
+    *p = fresh;
+    *cap = need;
+    return 0;
+}
+
 template <typename T>
 int ensure_pin(T** p, uint64_t* cap, uint64_t need) {
     if (*cap >= need) return 0;
@@ -175,9 +199,71 @@ int ensure_pin(T** p, uint64_t* cap, uint64_t need) {
     return 0;
 }
 
+// A cheap content check of a host weight buffer: 64-bit mix of its first and
+// last 4 KB and of 64 evenly spaced 64-byte samples (about 12 KB read per
+// call).  The residency cache compares it on every host call, so a buffer
+// freed and reallocated at the same address with the same size but other
+// bytes (a second model mapped where the first was) is uploaded again instead
+// of being served from the stale device copy.
+uint64_t content_fingerprint(const void* p, uint64_t n) {
+    const auto* b = static_cast<const uint8_t*>(p);
+    uint64_t h = 0x9E3779B97F4A7C15ull ^ n;
+    auto mix = [&h](const uint8_t* q, uint64_t len) {
+        uint64_t i = 0;
+        for (; i + 8 <= len; i += 8) {
+            uint64_t v;
+            std::memcpy(&v, q + i, 8);
+            h = (h ^ v) * 0xFF51AFD7ED558CCDull;
+            h ^= h >> 32;
+        }
+        for (; i < len; ++i) h = (h ^ q[i]) * 0x100000001B3ull;
+    };
+    const uint64_t edge = 4096;
+    if (n <= 2 * edge + 64 * 64) {
+        mix(b, n);
+        return h;
+    }
+    mix(b, edge);
+    mix(b + n - edge, edge);
+    const uint64_t step = (n - 2 * edge) / 64;
+    for (uint64_t k = 0; k < 64; ++k) mix(b + edge + k * step, 64);
+    return h;
+}
+
+// Host weight -> device through two pinned bounce buffers: the copy of chunk
+// i+1 into one buffer overlaps the DMA of chunk i from the other (a pageable
+// cudaMemcpy stages through a driver buffer one chunk at a time).
+constexpr uint64_t kUploadChunk = 8ull << 20;
+
+int upload_weight(DeviceState* s, void* dst, const void* src, uint64_t n) {
+    for (int k = 0; k < 2; ++k) {
+        if (s->upload_pin[k] == nullptr) {
+            NEDO_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&s->upload_pin[k]), kUploadChunk,
+                                        cudaHostAllocDefault));
+            NEDO_CUDA_TRY(cudaEventCreateWithFlags(&s->upload_done[k], cudaEventDisableTiming));
+        }
+    }
+    const auto* in = static_cast<const uint8_t*>(src);
+    auto* out = static_cast<uint8_t*>(dst);
+    uint64_t off = 0;
+    for (uint32_t i = 0; off < n; ++i) {
+        const uint32_t k = i & 1u;
+        const uint64_t len = n - off < kUploadChunk ? n - off : kUploadChunk;
+        // the DMA that last read this buffer is done before it is refilled
+        NEDO_CUDA_TRY(cudaEventSynchronize(s->upload_done[k]));
+        std::memcpy(s->upload_pin[k], in + off, len);
+        NEDO_CUDA_TRY(cudaMemcpyAsync(out + off, s->upload_pin[k], len, cudaMemcpyHostToDevice, s->stream));
+        NEDO_CUDA_TRY(cudaEventRecord(s->upload_done[k], s->stream));
+        off += len;
+    }
+    NEDO_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
 int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const void** w_dev) {
+    const uint64_t fp = content_fingerprint(w_host, w_bytes);
     auto it = s->cache.find(w_host);
-    if (it != s->cache.end() && it->second.bytes == w_bytes) {
+    if (it != s->cache.end() && it->second.bytes == w_bytes && it->second.fingerprint == fp) {
         *w_dev = it->second.dev;
         return 0;
     }
@@ -196,15 +282,15 @@ int resident_weight(DeviceState* s, const void* w_host, uint64_t w_bytes, const 
     }
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight)");
     if (w_bytes) {
-        e = cudaMemcpy(d, w_host, w_bytes, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
+        if (int rc = upload_weight(s, d, w_host, w_bytes)) {
             cudaFree(d);
-            return cuda_fail(e, "cudaMemcpy(weight upload)");
+            return rc;
         }
     }
     Resident r;
     r.dev = d;
     r.bytes = w_bytes;
+    r.fingerprint = fp;
     s->cache[w_host] = r;
     *w_dev = d;
     return 0;
@@ -248,26 +334,29 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
             return 0;
         }
     }
-    if (batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols && amax == nullptr && aligned16(w) &&
-        aligned16(x) && gemm_tc_supported(type, rows, cols, batch)) {
+    if (g_exact_batches.load() == 0 && batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols &&
+        amax == nullptr && aligned16(w) && aligned16(x) && gemm_tc_supported(type, rows, cols, batch)) {
         // tokens as the N dimension of a tcgen05 GEMM (x rounded to fp16 once)
         const uint64_t n = static_cast<uint64_t>(batch) * cols;
-        if (int rc = ensure_dev(&s->xh, &s->xh_cap, n)) return rc;
-        cudaError_t e = launch_x_to_f16(x, s->xh, n, s->num_sms, stream);
-        if (e != cudaSuccess) return cuda_fail(e, "x to fp16 launch");
         const uint32_t splits = gemm_tc_splits(rows, cols, batch, s->num_sms);
+        if (int rc = ensure_dev_retiring(s, &s->xh, &s->xh_cap, n)) return rc;
+        if (splits > 1) {
+            if (int rc = ensure_dev_retiring(s, &s->splitk_ws, &s->splitk_cap,
+                                             static_cast<uint64_t>(splits) * batch * rows))
+                return rc;
+        }
+        cudaError_t e = launch_x_to_f16(x, s->xh, n, s->num_sms, stream, use_pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "x to fp16 launch");
         if (splits > 1) {
             // few tiles: K shared among CTAs, partial sums folded in split order
-            if (int rc = ensure_dev(&s->splitk_ws, &s->splitk_cap, static_cast<uint64_t>(splits) * batch * rows))
-                return rc;
-            e = launch_gemm_tc(type, w, s->xh, s->splitk_ws, rows, cols, batch, rows, s->status, stream, splits,
-                               static_cast<uint64_t>(batch) * rows);
+            e = launch_gemm_tc(type, w, s->xh, s->splitk_ws, rows, cols, batch, rows, s->status, stream, use_pdl,
+                               splits, static_cast<uint64_t>(batch) * rows);
             if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
-            e = launch_splitk_reduce(s->splitk_ws, y, splits, batch, rows, rows, s->num_sms, stream);
+            e = launch_splitk_reduce(s->splitk_ws, y, splits, batch, rows, rows, s->num_sms, stream, use_pdl);
             if (e != cudaSuccess) return cuda_fail(e, "split-K fold launch");
             return 0;
         }
-        e = launch_gemm_tc(type, w, s->xh, y, rows, cols, batch, rows, s->status, stream);
+        e = launch_gemm_tc(type, w, s->xh, y, rows, cols, batch, rows, s->status, stream, use_pdl);
         if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
         return 0;
     }
@@ -314,13 +403,18 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
     return 0;
 }
 
+// Reset the failure flags and site of the device status word (its wait bound stays).
+void clear_status_flags(DeviceState* s, cudaStream_t stream) {
+    cudaMemsetAsync(s->status, 0, 2 * sizeof(uint32_t), stream);
+    cudaStreamSynchronize(stream);
+}
+
 int read_status(DeviceState* s, cudaStream_t stream) {
     NEDO_CUDA_TRY(cudaMemcpyAsync(s->status_pin, s->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, stream));
     NEDO_CUDA_TRY(cudaStreamSynchronize(stream));
     if (s->status_pin->flags != 0) {
         const DeviceStatus st = *s->status_pin;
-        cudaMemsetAsync(s->status, 0, sizeof(DeviceStatus), stream);
-        cudaStreamSynchronize(stream);
+        clear_status_flags(s, stream);
         char buf[160];
         std::snprintf(buf, sizeof(buf), "device kernel gave up on a bounded wait (flags=0x%x, site=%u)", st.flags,
                       st.where);
@@ -378,6 +472,8 @@ int nedo_gpu_set_pdl(int enable) {
     const int prev = g_pdl.exchange(enable != 0 ? 1 : 0);
     return prev;
 }
+
+int nedo_gpu_set_exact_batches(int enable) { return g_exact_batches.exchange(enable != 0 ? 1 : 0); }
 
 const char* nedo_gpu_last_error(void) { return g_last_error.c_str(); }
 
@@ -441,8 +537,7 @@ int nedo_gpu_matvec(uint32_t type, uint64_t rows, uint64_t cols, const void* w_h
     NEDO_CUDA_TRY(cudaStreamSynchronize(s->stream));
     if (s->status_pin->flags != 0) {
         const DeviceStatus st = *s->status_pin;
-        cudaMemsetAsync(s->status, 0, sizeof(DeviceStatus), s->stream);
-        cudaStreamSynchronize(s->stream);
+        clear_status_flags(s, s->stream);
         char buf[160];
         std::snprintf(buf, sizeof(buf), "device kernel gave up on a bounded wait (flags=0x%x, site=%u)", st.flags,
                       st.where);
@@ -505,8 +600,63 @@ int nedo_gpu_cache_clear(void) {
         cudaSetDevice(s->device);
         for (auto& kv : s->cache) release_resident(kv.second);
         s->cache.clear();
+        for (void* p : s->retired) cudaFree(p);
+        s->retired.clear();
     }
     cudaSetDevice(prev);
+    return 0;
+}
+
+int nedo_gpu_set_wait_limit_ns(uint64_t ns) {
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    NEDO_CUDA_TRY(cudaMemcpy(&s->status->wait_limit_ns, &ns, sizeof(ns), cudaMemcpyHostToDevice));
+    s->wait_limit_ns = ns;
+    return 0;
+}
+
+int nedo_gpu_reserve(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    if (rows == 0 || batch < tensor_core_min_batch(type) || cols < kTensorCoreMinCols ||
+        !gemm_tc_supported(type, rows, cols, batch))
+        return 0;  // this shape needs no shared buffer
+    if (int rc = ensure_dev_retiring(s, &s->xh, &s->xh_cap, static_cast<uint64_t>(batch) * cols)) return rc;
+    const uint32_t splits = gemm_tc_splits(rows, cols, batch, s->num_sms);
+    if (splits > 1)
+        if (int rc = ensure_dev_retiring(s, &s->splitk_ws, &s->splitk_cap,
+                                         static_cast<uint64_t>(splits) * batch * rows))
+            return rc;
+    return 0;
+}
+
+int nedo_gpu_matvec_batch(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                          const float* x_host, float* y_host, uint32_t batch) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0 || batch == 0) return 0;
+    if (!w_host || !x_host || !y_host) return fail(NEDO_GPU_ERR_ARG, "matvec_batch: null pointer");
+    if (w_bytes < rows * rb) return fail(NEDO_GPU_ERR_ARG, "matvec: weight span shorter than rows * row_bytes");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    const void* w_dev = nullptr;
+    if (int rc = resident_weight(s, w_host, w_bytes, &w_dev)) return rc;
+    const uint64_t nx = static_cast<uint64_t>(batch) * cols, ny = static_cast<uint64_t>(batch) * rows;
+    if (int rc = ensure_dev(&s->x_dev, &s->x_cap, nx)) return rc;
+    if (int rc = ensure_dev(&s->y_dev, &s->y_cap, ny)) return rc;
+    if (int rc = ensure_pin(&s->x_pin, &s->xp_cap, nx)) return rc;
+    if (int rc = ensure_pin(&s->y_pin, &s->yp_cap, ny)) return rc;
+    std::memcpy(s->x_pin, x_host, nx * sizeof(float));
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->x_dev, s->x_pin, nx * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, batch, nullptr, s->stream, 0))
+        return rc;
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->y_pin, s->y_dev, ny * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (int rc = read_status(s, s->stream)) return rc;
+    std::memcpy(y_host, s->y_pin, ny * sizeof(float));
     return 0;
 }
 
@@ -643,8 +793,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
-    const bool tc = batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols &&
-                    gemm_tc_supported(type, rows, cols, batch);
+    const bool tc = g_exact_batches.load() == 0 && batch >= tensor_core_min_batch(type) &&
+                    cols >= kTensorCoreMinCols && gemm_tc_supported(type, rows, cols, batch);
     if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
         const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, tokens);
@@ -679,6 +829,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
         out[1] = gemm_tc_launch_ctas(type, rows, cols, batch, s->num_sms);
         out[2] = 320;
         out[4] = 128;
+        out[5] = gemm_tc_splits(rows, cols, batch, s->num_sms);  // K splits (> 1: a fold kernel follows)
         return 0;
     }
     out[0] = batch > 1 ? 3 : 2;

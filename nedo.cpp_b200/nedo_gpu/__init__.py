@@ -34,13 +34,17 @@ OK, ERR_TYPE, ERR_ALIGN, ERR_ROW, ERR_ARG, ERR_CUDA, ERR_DEVICE, ERR_NOMEM = ran
 EXPORTS = (
     "nedo_gpu_version",
     "nedo_gpu_set_pdl",
+    "nedo_gpu_set_exact_batches",
     "nedo_gpu_last_error",
+    "nedo_gpu_set_wait_limit_ns",
     "nedo_gpu_matvec",
+    "nedo_gpu_matvec_batch",
     "nedo_gpu_embedding_row",
     "nedo_gpu_weight_upload",
     "nedo_gpu_weight_evict",
     "nedo_gpu_cache_clear",
     "nedo_gpu_matvec_dev",
+    "nedo_gpu_reserve",
     "nedo_gpu_matvec_argmax_dev",
     "nedo_gpu_argmax_dev",
     "nedo_gpu_argmax_dev_noalloc",
@@ -67,13 +71,17 @@ _u64p = ctypes.POINTER(ctypes.c_uint64)
 _SIGNATURES = {
     "nedo_gpu_version": ([], _i32),
     "nedo_gpu_set_pdl": ([_i32], _i32),
+    "nedo_gpu_set_exact_batches": ([_i32], _i32),
     "nedo_gpu_last_error": ([], ctypes.c_char_p),
+    "nedo_gpu_set_wait_limit_ns": ([_u64], _i32),
     "nedo_gpu_matvec": ([_u32, _u64, _u64, _vp, _u64, _vp, _vp], _i32),
+    "nedo_gpu_matvec_batch": ([_u32, _u64, _u64, _vp, _u64, _vp, _vp, _u32], _i32),
     "nedo_gpu_embedding_row": ([_u32, _u64, _u64, _vp, _u64, _u32, _vp], _i32),
     "nedo_gpu_weight_upload": ([_vp, _u64, ctypes.POINTER(_vp)], _i32),
     "nedo_gpu_weight_evict": ([_vp], _i32),
     "nedo_gpu_cache_clear": ([], _i32),
     "nedo_gpu_matvec_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _u32, _vp], _i32),
+    "nedo_gpu_reserve": ([_u32, _u64, _u64, _u32], _i32),
     "nedo_gpu_matvec_argmax_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev": ([_vp, _u64, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev_noalloc": ([_vp, _u64, _vp, _vp, _vp], _i32),
@@ -107,8 +115,16 @@ class Library:
         """Programmatic dependent launch for the device entry points; returns the old setting."""
         return bool(self.lib.nedo_gpu_set_pdl(1 if enable else 0))
 
+    def set_exact_batches(self, enable: bool) -> bool:
+        """Batched calls on the exact kernels only (no fp16 tensor-core GEMM); returns the old setting."""
+        return bool(self.lib.nedo_gpu_set_exact_batches(1 if enable else 0))
+
     def last_error(self) -> str:
         return self.lib.nedo_gpu_last_error().decode()
+
+    def set_wait_limit_ns(self, ns: int) -> None:
+        """Bound of the kernels' spin-waits on the current device (0 = default 2 s)."""
+        self._check(self.lib.nedo_gpu_set_wait_limit_ns(ns))
 
     def _check(self, rc: int) -> None:
         if rc != OK:
@@ -125,6 +141,18 @@ class Library:
         # raw addresses from the array interface (cheaper than .ctypes per call)
         self._check(self.lib.nedo_gpu_matvec(type_, rows, cols, w.__array_interface__["data"][0], w.nbytes,
                                              x.__array_interface__["data"][0], y.__array_interface__["data"][0]))
+        return y
+
+    def matvec_batch(self, type_: int, rows: int, cols: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+        """`x.shape[0]` matvecs over one weight: y[b] = W @ x[b] (x [batch, cols])."""
+        if not (isinstance(w, np.ndarray) and w.flags.c_contiguous):
+            w = np.ascontiguousarray(w)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != cols:
+            raise ValueError("x must be [batch, cols]")
+        y = np.empty((x.shape[0], rows), dtype=np.float32)
+        self._check(self.lib.nedo_gpu_matvec_batch(type_, rows, cols, w.__array_interface__["data"][0], w.nbytes,
+                                                   x.ctypes.data, y.ctypes.data, x.shape[0]))
         return y
 
     def embedding_row(self, type_: int, rows: int, cols: int, w: np.ndarray, row: int) -> np.ndarray:
@@ -149,6 +177,10 @@ class Library:
     # ----------------------------------------------------- device entry points
     def matvec_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, batch=1, stream=0) -> None:
         self._check(self.lib.nedo_gpu_matvec_dev(type_, rows, cols, w_ptr, x_ptr, y_ptr, batch, stream))
+
+    def reserve(self, type_, rows, cols, batch) -> None:
+        """Size the buffers of a batched matvec_dev of this shape (call before graph capture)."""
+        self._check(self.lib.nedo_gpu_reserve(type_, rows, cols, batch))
 
     def matvec_argmax_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, index_ptr, value_ptr=None, stream=0) -> None:
         self._check(self.lib.nedo_gpu_matvec_argmax_dev(type_, rows, cols, w_ptr, x_ptr, y_ptr, index_ptr,

@@ -98,3 +98,28 @@ def gen_x(cols: int, seed: int, batch: int | None = None) -> np.ndarray:
     rng = np.random.default_rng(seed + 1_000_003)
     shape = (cols,) if batch is None else (batch, cols)
     return rng.standard_normal(size=shape, dtype=np.float32)
+
+
+def gen_weight_torch(torch, type_: int, rows: int, cols: int, copies: int, seed: int, device):
+    """`copies` independent seeded weights ``[copies, rows * row_bytes]`` (uint8)
+    generated on `device` with torch's generator, in the distributions of
+    ``gen_weight`` (for sizes where numpy generation would be slow).  The bytes
+    differ from ``gen_weight``'s for the same seed; a checker reads them back."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    nb = cols // 32
+    if type_ == F16:
+        w = (torch.randn((copies, rows, cols), generator=g, device=device) * 0.02).half()
+        return w.view(torch.uint8).reshape(copies, -1)
+    bb = BLOCK_BYTES[type_]
+    blk = torch.empty((copies, rows, nb, bb), dtype=torch.uint8, device=device)
+    if type_ == Q8_0:
+        q = torch.randint(-127, 128, (copies, rows, nb, 32), generator=g, device=device, dtype=torch.int16)
+        blk[..., 2:] = q.to(torch.int8).view(torch.uint8)
+        d = (torch.randn((copies, rows, nb), generator=g, device=device).abs() * (0.02 / 127.0)).half()
+    else:
+        blk[..., 2:] = torch.randint(0, 256, (copies, rows, nb, 16), generator=g, device=device,
+                                     dtype=torch.int16).to(torch.uint8)
+        d = (torch.randn((copies, rows, nb), generator=g, device=device).abs() * (0.02 / 8.0)).half()
+    blk[..., 0:2] = d.contiguous().view(torch.uint8).reshape(copies, rows, nb, 2)
+    return blk.reshape(copies, -1)
