@@ -201,6 +201,31 @@ NEDO_GPU_API int nedo_gpu_argmax_dev(const float* v_dev, uint64_t n, int64_t* in
 NEDO_GPU_API int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_dev, float* value_dev,
                                 void* stream);
 
+/* The k largest elements of an fp32 vector in device memory, largest first
+ * (equal values: smaller index first; NaN never ahead of a number):
+ * ids_dev[0..k) (uint32) and vals_dev[0..k) (may be NULL).  1 <= k <= 256 and
+ * k <= n.  This is the candidate selection of the reference's sampler
+ * (sample_token, src/model.cpp:38-44: nth_element + sort by logit), done where
+ * the logits are.  Uses a per-device scratch area: calls that overlap on the
+ * GPU must not share a device. */
+NEDO_GPU_API int nedo_gpu_topk_dev(const float* v_dev, uint64_t n, uint32_t k, uint32_t* ids_dev, float* vals_dev,
+                                   void* stream);
+
+/* Host-pointer LM head (the matvec of src/model.cpp:259, nedo_gpu_matvec's
+ * residency and errors) followed by the top k logits (nedo_gpu_topk_dev), with
+ * only the k (id, logit) pairs copied back instead of all `rows` logits:
+ * ids_host[0..k), vals_host[0..k) (may be NULL).  1 <= k <= min(rows, 256). */
+NEDO_GPU_API int nedo_gpu_lm_head_topk(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host,
+                                       uint64_t w_bytes, const float* x_host, uint32_t k, uint32_t* ids_host,
+                                       float* vals_host);
+
+/* Host-pointer LM head with the greedy pick (src/model.cpp:36, std::max_element
+ * semantics as nedo_gpu_argmax_dev), fused into the matvec where the shape
+ * allows: *index_host, *value_host (may be NULL); no logits are copied back. */
+NEDO_GPU_API int nedo_gpu_lm_head_argmax(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host,
+                                         uint64_t w_bytes, const float* x_host, int64_t* index_host,
+                                         float* value_host);
+
 /* Row-sharded matvec with the all-gather of y fused into it (one process
  * per GPU; rows are independent, src/kernels.cpp:166-168).  Computes this
  * rank's rows into y_dev like nedo_gpu_matvec_dev and also stores each row at

@@ -104,6 +104,41 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr,
                         uint64_t ldx = 0, uint64_t ldy = 0);
 
+// Batch-1 Q8_0 / Q4_0 on tcgen05 (kind::i8, A from TMEM): 16-row tiles, one
+// MMA per 8 blocks of a tile (M = 16 rows x 8 blocks), at most ~110 KB of
+// shared memory and 256 TMEM columns per CTA so that two launches share an SM.
+// Rows of a multiple of 256 elements, at most 8192.
+struct Tc8Plan {
+    bool ok = false;
+    uint32_t type = 0;
+    uint64_t rows = 0, cols = 0;
+    uint32_t grid = 0;
+    uint32_t threads = 0;
+    uint32_t slots = 0;        // ring slots (units of 16 rows x 16 blocks)
+    uint32_t unit_bytes = 0;
+    uint32_t tiles = 0;
+    uint32_t steps = 0;        // K steps (8 blocks) per row
+    uint32_t units = 0;        // units per tile
+    uint32_t off_table = 0, off_consts = 0, off_sd = 0, off_red = 0, off_bars = 0;
+    uint32_t smem_bytes = 0;
+};
+Tc8Plan plan_tc8(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin);
+cudaError_t launch_tc8(const Tc8Plan& plan, const void* w, const float* x, float* y, DeviceStatus* status,
+                       cudaStream_t stream, bool pdl);
+
+// Top-k of an fp32 vector (k <= kTopkMax): ids[0..k) and vals[0..k) by value
+// descending, equal values by smaller index first, NaN never ahead of a number.
+constexpr uint32_t kTopkMax = 256;
+struct TopkScratch {
+    uint64_t* cand;     // [ctas x 256] candidate keys
+    uint32_t* counter;  // starts at 0, reset to 0 by the last CTA
+    uint32_t* ids;      // result
+    float* vals;        // result (may be null)
+};
+uint32_t topk_ctas(uint64_t n, uint32_t k, int num_sms);
+cudaError_t launch_topk(const float* v, uint64_t n, uint32_t k, const TopkScratch& s, int num_sms,
+                        cudaStream_t stream);
+
 // One thread waits (bounded, 2 s) until *signal has advanced by `increment`
 // past *expected, then advances *expected: the peers' rows are visible after it.
 cudaError_t launch_gather_wait(uint32_t* signal, uint32_t* expected, uint32_t increment, DeviceStatus* status,

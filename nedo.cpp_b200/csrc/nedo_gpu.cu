@@ -68,6 +68,14 @@ struct DeviceState {
     int max_smem = 0;
     DeviceStatus* status = nullptr;  // device memory
     ArgmaxScratch scratch{};
+    uint64_t* topk_cand = nullptr;   // [num_sms x kTopkMax] candidate keys of the top-k kernel
+    uint32_t* topk_counter = nullptr;
+    uint32_t* topk_ids = nullptr;    // [kTopkMax] results of the host LM-head entry points
+    float* topk_vals = nullptr;
+    int64_t* amax_index = nullptr;
+    float* amax_value = nullptr;
+    uint32_t* topk_ids_pin = nullptr;
+    float* topk_vals_pin = nullptr;
     cudaStream_t stream = nullptr;   // for the host-pointer entry points
     float* x_dev = nullptr;
     float* y_dev = nullptr;
@@ -123,6 +131,16 @@ int get_state(DeviceState** out) {
     NEDO_CUDA_TRY(cudaMemset(s->scratch.counter, 0, sizeof(uint32_t)));
     NEDO_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
     NEDO_CUDA_TRY(cudaHostAlloc(&s->status_pin, sizeof(DeviceStatus), cudaHostAllocDefault));
+    NEDO_CUDA_TRY(cudaMalloc(&s->topk_cand, static_cast<size_t>(s->num_sms) * kTopkMax * sizeof(uint64_t)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->topk_counter, sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaMemset(s->topk_counter, 0, sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->topk_ids, kTopkMax * sizeof(uint32_t)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->topk_vals, kTopkMax * sizeof(float)));
+    NEDO_CUDA_TRY(cudaMalloc(&s->amax_index, sizeof(int64_t) + sizeof(float)));
+    s->amax_value = reinterpret_cast<float*>(s->amax_index + 1);
+    NEDO_CUDA_TRY(cudaHostAlloc(&s->topk_ids_pin, kTopkMax * (sizeof(uint32_t) + sizeof(float)) + 16,
+                                cudaHostAllocDefault));
+    s->topk_vals_pin = reinterpret_cast<float*>(s->topk_ids_pin + kTopkMax);
     g_states[dev] = s;
     *out = s;
     return 0;
@@ -313,11 +331,31 @@ constexpr uint32_t kTensorCoreMinBatchF16 = 4;
 uint32_t tensor_core_min_batch(uint32_t type) { return type == kF16 ? kTensorCoreMinBatchF16 : kTensorCoreMinBatch; }
 constexpr uint64_t kTensorCoreMinCols = 1024;
 
+// The tcgen05 batch-1 kernel (gemv_tc8.cu) for the shapes it takes, when the
+// environment variable NEDO_GPU_TC8=1 is set (otherwise the int8 mma.sync
+// kernel of gemv_imma.cu runs them).
+bool tc8_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("NEDO_GPU_TC8");
+        return v != nullptr && std::strcmp(v, "1") == 0;
+    }();
+    return on;
+}
+
 // The one dispatch point for every matvec launch.
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
                     float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream, int pdl_override = -1) {
     if (rows == 0 || batch == 0) return 0;
     const bool use_pdl = pdl_override < 0 ? g_pdl.load() != 0 : pdl_override != 0;
+    if (batch == 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0) &&
+        tc8_enabled()) {
+        Tc8Plan tp = plan_tc8(type, rows, cols, s->num_sms, s->max_smem);
+        if (tp.ok) {
+            cudaError_t e = launch_tc8(tp, w, x, y, s->status, stream, use_pdl);
+            if (e != cudaSuccess) return cuda_fail(e, "gemv_tc8 launch");
+            return 0;
+        }
+    }
     if (batch == 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
         if (ip.ok) {
@@ -725,6 +763,88 @@ int nedo_gpu_argmax_dev_noalloc(const float* v_dev, uint64_t n, int64_t* index_d
     return 0;
 }
 
+int nedo_gpu_topk_dev(const float* v_dev, uint64_t n, uint32_t k, uint32_t* ids_dev, float* vals_dev, void* stream) {
+    if (n == 0) return fail(NEDO_GPU_ERR_ARG, "topk of an empty vector");
+    if (n > 0xFFFFFFFFull) return fail(NEDO_GPU_ERR_ARG, "topk: more than 2^32-1 elements");
+    if (k == 0 || k > kTopkMax || k > n)
+        return fail(NEDO_GPU_ERR_ARG, "topk: k must be in [1, min(n, " + std::to_string(kTopkMax) + ")]");
+    if (!v_dev || !ids_dev) return fail(NEDO_GPU_ERR_ARG, "topk_dev: null pointer");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    TopkScratch t{s->topk_cand, s->topk_counter, ids_dev, vals_dev};
+    cudaError_t e = launch_topk(v_dev, n, k, t, s->num_sms, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "topk launch");
+    return 0;
+}
+
+// Host-pointer LM head: x up, the matvec into the library's device y, then the
+// greedy pick (k == 0) or the top k logits; only the result comes back.
+static int lm_head_host(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                 const float* x_host, uint32_t k, uint32_t* ids_host, float* vals_host, int64_t* index_host,
+                 float* value_host) {
+    uint64_t rb = 0;
+    if (int rc = check_matvec_args(type, rows, cols, &rb)) return rc;
+    if (rows == 0) return fail(NEDO_GPU_ERR_ARG, "LM head with no rows");
+    if (!w_host || !x_host) return fail(NEDO_GPU_ERR_ARG, "lm_head: null pointer");
+    if (w_bytes < rows * rb) return fail(NEDO_GPU_ERR_ARG, "matvec: weight span shorter than rows * row_bytes");
+    if (k > kTopkMax || k > rows)
+        return fail(NEDO_GPU_ERR_ARG, "lm_head_topk: k must be in [1, min(rows, " + std::to_string(kTopkMax) + ")]");
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    std::lock_guard<std::mutex> lk(s->mu);
+    const void* w_dev = nullptr;
+    if (int rc = resident_weight(s, w_host, w_bytes, &w_dev)) return rc;
+    if (int rc = ensure_dev(&s->x_dev, &s->x_cap, cols)) return rc;
+    if (int rc = ensure_dev(&s->y_dev, &s->y_cap, rows)) return rc;
+    if (int rc = ensure_pin(&s->x_pin, &s->xp_cap, cols)) return rc;
+    std::memcpy(s->x_pin, x_host, cols * sizeof(float));
+    NEDO_CUDA_TRY(cudaMemcpyAsync(s->x_dev, s->x_pin, cols * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    if (k == 0) {
+        ArgmaxScratch a = s->scratch;
+        a.out_index = s->amax_index;
+        a.out_value = s->amax_value;
+        if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, 1, &a, s->stream, 0)) return rc;
+        NEDO_CUDA_TRY(cudaMemcpyAsync(s->topk_ids_pin, s->amax_index, sizeof(int64_t) + sizeof(float),
+                                      cudaMemcpyDeviceToHost, s->stream));
+    } else {
+        if (int rc = dispatch_matvec(s, type, rows, cols, w_dev, s->x_dev, s->y_dev, 1, nullptr, s->stream, 0))
+            return rc;
+        TopkScratch t{s->topk_cand, s->topk_counter, s->topk_ids, s->topk_vals};
+        cudaError_t e = launch_topk(s->y_dev, rows, k, t, s->num_sms, s->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "topk launch");
+        NEDO_CUDA_TRY(cudaMemcpyAsync(s->topk_ids_pin, s->topk_ids, k * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                      s->stream));
+        NEDO_CUDA_TRY(cudaMemcpyAsync(s->topk_vals_pin, s->topk_vals, k * sizeof(float), cudaMemcpyDeviceToHost,
+                                      s->stream));
+    }
+    if (int rc = read_status(s, s->stream)) return rc;
+    if (k == 0) {
+        int64_t idx;
+        float val;
+        std::memcpy(&idx, s->topk_ids_pin, sizeof(idx));
+        std::memcpy(&val, reinterpret_cast<const uint8_t*>(s->topk_ids_pin) + sizeof(idx), sizeof(val));
+        if (index_host) *index_host = idx;
+        if (value_host) *value_host = val;
+    } else {
+        std::memcpy(ids_host, s->topk_ids_pin, k * sizeof(uint32_t));
+        if (vals_host) std::memcpy(vals_host, s->topk_vals_pin, k * sizeof(float));
+    }
+    return 0;
+}
+
+int nedo_gpu_lm_head_topk(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                          const float* x_host, uint32_t k, uint32_t* ids_host, float* vals_host) {
+    if (k == 0) return fail(NEDO_GPU_ERR_ARG, "lm_head_topk: k must be in [1, min(rows, 256)]");
+    if (!ids_host) return fail(NEDO_GPU_ERR_ARG, "lm_head_topk: null pointer");
+    return lm_head_host(type, rows, cols, w_host, w_bytes, x_host, k, ids_host, vals_host, nullptr, nullptr);
+}
+
+int nedo_gpu_lm_head_argmax(uint32_t type, uint64_t rows, uint64_t cols, const void* w_host, uint64_t w_bytes,
+                            const float* x_host, int64_t* index_host, float* value_host) {
+    if (!index_host) return fail(NEDO_GPU_ERR_ARG, "lm_head_argmax: null pointer");
+    return lm_head_host(type, rows, cols, w_host, w_bytes, x_host, 0, nullptr, nullptr, index_host, value_host);
+}
+
 int nedo_gpu_matvec_allgather_dev(uint32_t type, uint64_t rows, uint64_t cols, const void* w_dev, const float* x_dev,
                                   float* y_dev, const uint64_t* peer_y, const uint64_t* peer_signal, uint32_t npeers,
                                   uint64_t row_offset, void* stream) {
@@ -795,6 +915,20 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
     const bool tc = g_exact_batches.load() == 0 && batch >= tensor_core_min_batch(type) &&
                     cols >= kTensorCoreMinCols && gemm_tc_supported(type, rows, cols, batch);
+    if (batch <= 1 && (type == kQ8_0 || type == kQ4_0) && tc8_enabled()) {
+        Tc8Plan tp = plan_tc8(type, rows, cols, s->num_sms, s->max_smem);
+        if (tp.ok) {
+            out[0] = 6;
+            out[1] = tp.grid;
+            out[2] = tp.threads;
+            out[3] = tp.smem_bytes;
+            out[4] = 16;
+            out[5] = tp.slots;
+            out[6] = tp.unit_bytes;
+            out[7] = 8;  // loader + epilogue warps
+            return 0;
+        }
+    }
     if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
         const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, tokens);

@@ -48,6 +48,9 @@ EXPORTS = (
     "nedo_gpu_matvec_argmax_dev",
     "nedo_gpu_argmax_dev",
     "nedo_gpu_argmax_dev_noalloc",
+    "nedo_gpu_topk_dev",
+    "nedo_gpu_lm_head_topk",
+    "nedo_gpu_lm_head_argmax",
     "nedo_gpu_matvec_allgather_dev",
     "nedo_gpu_allgather_wait_dev",
     "nedo_gpu_dequant_rows_dev",
@@ -85,6 +88,9 @@ _SIGNATURES = {
     "nedo_gpu_matvec_argmax_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev": ([_vp, _u64, _vp, _vp, _vp], _i32),
     "nedo_gpu_argmax_dev_noalloc": ([_vp, _u64, _vp, _vp, _vp], _i32),
+    "nedo_gpu_topk_dev": ([_vp, _u64, _u32, _vp, _vp, _vp], _i32),
+    "nedo_gpu_lm_head_topk": ([_u32, _u64, _u64, _vp, _u64, _vp, _u32, _vp, _vp], _i32),
+    "nedo_gpu_lm_head_argmax": ([_u32, _u64, _u64, _vp, _u64, _vp, _vp, _vp], _i32),
     "nedo_gpu_matvec_allgather_dev": ([_u32, _u64, _u64, _vp, _vp, _vp, _u64p, _u64p, _u32, _u64, _vp], _i32),
     "nedo_gpu_allgather_wait_dev": ([_vp, _vp, _u32, _vp], _i32),
     "nedo_gpu_dequant_rows_dev": ([_u32, _u64, _u64, _vp, _u64, _u64, _vp, _vp], _i32),
@@ -193,6 +199,30 @@ class Library:
         """argmax_dev with no allocation (a fixed device array of the library;
         overlapping calls on one device race; first call outside stream capture)."""
         self._check(self.lib.nedo_gpu_argmax_dev_noalloc(v_ptr, n, index_ptr, value_ptr, stream))
+
+    def topk_dev(self, v_ptr, n, k, ids_ptr, vals_ptr=None, stream=0) -> None:
+        """The k largest of a device fp32 vector: ids (uint32) and values, largest first."""
+        self._check(self.lib.nedo_gpu_topk_dev(v_ptr, n, k, ids_ptr, vals_ptr, stream))
+
+    def lm_head_topk(self, type_, rows, cols, w: np.ndarray, x: np.ndarray, k: int):
+        """LM head (host pointers) + the top k logits: (ids uint32 [k], logits float32 [k])."""
+        w = np.ascontiguousarray(w)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        ids = np.empty(k, dtype=np.uint32)
+        vals = np.empty(k, dtype=np.float32)
+        self._check(self.lib.nedo_gpu_lm_head_topk(type_, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data, k,
+                                                   ids.ctypes.data, vals.ctypes.data))
+        return ids, vals
+
+    def lm_head_argmax(self, type_, rows, cols, w: np.ndarray, x: np.ndarray):
+        """LM head (host pointers) + the greedy pick: (index, logit)."""
+        w = np.ascontiguousarray(w)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        idx = ctypes.c_int64(-1)
+        val = ctypes.c_float(0.0)
+        self._check(self.lib.nedo_gpu_lm_head_argmax(type_, rows, cols, w.ctypes.data, w.nbytes, x.ctypes.data,
+                                                     ctypes.byref(idx), ctypes.byref(val)))
+        return idx.value, val.value
 
     def matvec_allgather_dev(self, type_, rows, cols, w_ptr, x_ptr, y_ptr, peer_y, peer_signal, row_offset,
                              stream=0) -> None:
