@@ -23,20 +23,23 @@
 // So every lane of the MMA does useful work on exactly one (row, block) pair,
 // and a tile is 16 rows: 11008 rows make 688 tiles for 148 SMs.
 //
-// Streaming.  A unit is 16 rows x 16 blocks (two K steps): one 2D tensor-map
-// copy (no multicast) into a shared-memory ring.  Roles (10 warps):
-//   warp 0      producer: issues every unit's copy as ring slots free up;
-//   warp 1      TMEM allocation and the MMA issuer (one thread);
-//   warps 2-5   loaders, one TMEM lane quarter each: read a unit's blocks from
-//               the ring (row r, block p per lane), expand Q4_0 nibbles, store
-//               the A tiles into TMEM (tcgen05.st) and the block scales d;
-//   warps 6-9   build the x limb table once x is available, then the epilogue:
-//               read each K step's D (tcgen05.ld), combine the limbs with
-//               d * 2^-e, accumulate per (row, block phase) and, per tile, add
-//               the 8 block phases of every row in a fixed order.
+// Streaming.  A unit is 16 rows x 16 blocks (two K steps); a ring slot holds
+// two units, brought in by one 2D tensor-map copy (no multicast).  Roles
+// (18 warps):
+//   warp 0       producer: issues every slot's copy as ring slots free up;
+//   warp 1       TMEM allocation and the MMA issuer (one thread);
+//   warps 2-9    loaders, one per (TMEM lane quarter, K step of a unit): read
+//                their lanes' blocks from the ring (row r, block p per lane),
+//                expand Q4_0 nibbles, store the A tile into TMEM (tcgen05.st)
+//                and the block scales d;
+//   warps 10-17  build the x limb table once x is available, then the epilogue,
+//                one per (lane quarter, K step): read the K step's D
+//                (tcgen05.ld), combine the limbs with d * 2^-e, accumulate per
+//                (row, block phase) and, per tile, add each row's 16 partial
+//                sums in a fixed order.
 // The weights do not depend on earlier kernels, so the copies and the A tiles
 // of the first units are prepared before griddepcontrol.wait; x is read after
-// it.  A CTA takes at most ~110 KB of shared memory, 320 threads x 96
+// it.  A CTA takes at most ~110 KB of shared memory, 576 threads x 56
 // registers and 256 TMEM columns, so under programmatic dependent launch the
 // next launch's CTA streams its weight on the same SM while this one finishes.
 // Every wait is bounded; a CTA-wide abort flag stops every role after the
@@ -54,6 +57,7 @@ constexpr uint32_t kTileRows = 16;
 constexpr uint32_t kPhases = 8;          // blocks per K step (block phases of a tile)
 constexpr uint32_t kUnitSteps = 2;       // K steps per unit
 constexpr uint32_t kUnitBlocks = kPhases * kUnitSteps;
+constexpr uint32_t kSlotUnits = 2;       // units per ring slot (one tensor-map copy: 32 blocks)
 constexpr uint32_t kN = 32;              // MMA N: 8 blocks x 4 limbs
 constexpr uint32_t kNA = 4;              // A buffers (units) in TMEM: 16 columns each
 constexpr uint32_t kND = 3;              // D buffers (units) in TMEM: 64 columns each
@@ -61,7 +65,7 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kACol0 = 0;
 constexpr uint32_t kDCol0 = kNA * 16u;
 static_assert(kDCol0 + kND * kUnitSteps * kN <= kTmemCols, "TMEM budget");
-constexpr uint32_t kThreads = 320;
+constexpr uint32_t kThreads = 576;  // 18 warps
 constexpr uint32_t kMaxSlots = 48;
 constexpr uint32_t kMaxSteps = 32;       // K steps per row the x table holds (8192 columns)
 constexpr uint32_t kStepTableBytes = 1024;  // 8 blocks x 4 limbs x 32 bytes
@@ -122,14 +126,11 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// This warp's 32 TMEM lanes, 16 consecutive columns from taddr: thread i writes lane i.
-__device__ __forceinline__ void tc_st_x16(uint32_t taddr, const uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
+// This warp's 32 TMEM lanes, 8 consecutive columns from taddr: thread i writes lane i.
+__device__ __forceinline__ void tc_st_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tc_ld_x8(uint32_t taddr, uint32_t (&v)[8]) {
@@ -158,14 +159,15 @@ __host__ __device__ constexpr uint32_t idesc_i8() {
 
 // Bounded wait on an mbarrier phase that also gives up when another role has
 // aborted (the flag is set by the first wait that ran out).
-// The waits of this kernel are on short, latency-critical hand-offs between
-// roles (often completed by tcgen05.commit), so they poll without a suspend
-// hint: a hinted wait may sleep for its whole hint after the phase completes.
-__device__ __forceinline__ bool try_wait_nohint(uint64_t* bar, uint32_t parity) {
+// The waits of this kernel are short, latency-critical hand-offs between roles
+// (several completed by tcgen05.commit).  A try_wait may suspend the thread for
+// an implementation-defined time before it notices the completed phase (about
+// 0.5 us measured here), so they poll test_wait instead.
+__device__ __forceinline__ bool test_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(parity)
@@ -175,11 +177,14 @@ __device__ __forceinline__ bool try_wait_nohint(uint64_t* bar, uint32_t parity) 
 
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                            DeviceStatus* st, uint32_t site) {
-    if (try_wait_nohint(bar, parity)) return true;
+    if (test_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     const uint64_t limit = wait_limit_ns(st);
-    while (true) {
-        if (try_wait_nohint(bar, parity)) return true;
+    for (uint32_t spin = 0;; ++spin) {
+        // poll back to back for the first few microseconds (a hand-off), then
+        // with a short sleep (a long wait, e.g. for the previous kernel)
+        if (spin >= 128u) __nanosleep(64);
+        if (test_wait(bar, parity)) return true;
         if (*abort_flag != 0u) return false;
         if (global_timer_ns() - t0 > limit) {
             if (st != nullptr && atomicOr(&st->flags, kErrWaitTimeout) == 0u) st->where = site;
@@ -264,16 +269,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     gemv_tc8_kernel(const __grid_constant__ CUtensorMap map, const Tc8Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr uint32_t BB = Blk<TYPE>::kBytes;
-    constexpr uint32_t kURB = kUnitBlocks * BB;          // data bytes per unit row: 544 or 288
-    constexpr uint32_t kPitch = kURB + 16u;               // its shared-memory pitch: 560 or 304
-    constexpr uint32_t kUnitBytes = kTileRows * kPitch;  // 8960 or 4864
+    constexpr uint32_t kSRB = kSlotUnits * kUnitBlocks * BB;  // data bytes per slot row: 1088 or 576
+    constexpr uint32_t kPitch = kSRB + 16u;                    // its shared-memory pitch: 1104 or 592
+    constexpr uint32_t kSlotBytes = kTileRows * kPitch;        // 17664 or 9472
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t S = a.slots;
 
     uint8_t* const table = smem + a.off_table;
     float4* const consts = reinterpret_cast<float4*>(smem + a.off_consts);
     float* const sd = reinterpret_cast<float*>(smem + a.off_sd);    // [kNA][2][128] block scales d
-    float* const red = reinterpret_cast<float*>(smem + a.off_red);  // [2][4][16] per-tile partial sums
+    float* const red = reinterpret_cast<float*>(smem + a.off_red);  // [2][8][16] per-tile partial sums
     uint64_t* const ring_full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
     uint64_t* const ring_empty = ring_full + S;
     uint64_t* const a_full = ring_empty + S;
@@ -291,25 +296,28 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * blockIdx.x / gridDim.x);
     const uint32_t tile_end = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * (blockIdx.x + 1) / gridDim.x);
     const uint32_t my_tiles = tile_end - tile_begin;
-    const uint32_t total = my_tiles * a.units;  // units of this CTA, tile-major
+    const uint32_t units = a.units;                    // compute units per tile (2 K steps each)
+    const uint32_t spt = (units + kSlotUnits - 1) / kSlotUnits;  // ring slots (copies) per tile
+    const uint32_t total = my_tiles * units;           // compute units of this CTA, tile-major
+    const uint32_t copies = my_tiles * spt;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&ring_full[s], 1);
-            mbar_init(&ring_empty[s], 4);  // the four loader warps
+            mbar_init(&ring_empty[s], 16);  // 8 loader warps x 2 units (a lone unit arrives twice)
         }
         for (uint32_t s = 0; s < kNA; ++s) {
-            mbar_init(&a_full[s], 4);
-            mbar_init(&a_free[s], 4);  // the four epilogue warps
+            mbar_init(&a_full[s], 8);  // the eight loader warps
+            mbar_init(&a_free[s], 8);  // the eight epilogue warps
         }
         for (uint32_t s = 0; s < kND; ++s) {
             mbar_init(&d_full[s], 1);
-            mbar_init(&d_free[s], 4);
+            mbar_init(&d_free[s], 8);
         }
-        mbar_init(table_full, 4);
+        mbar_init(table_full, 8);
         mbar_init(mma_done, 1);
         for (uint32_t s = 0; s < 2; ++s) {
-            mbar_init(&red_full[s], 4);
+            mbar_init(&red_full[s], 8);
             mbar_init(&red_free[s], 1);
         }
         *abort_flag = 0u;
@@ -333,17 +341,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ---------------- producer ----------------
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
-            uint32_t issued = 0;
-            for (uint32_t u = 0; u < total; ++u) {
-                const uint32_t slot = u % S;
-                if (u >= S && !wait_phase(&ring_empty[slot], ((u / S) - 1u) & 1u, abort_flag, a.status, 61u)) break;
-                const uint32_t t = u / a.units, uk = u - t * a.units;
-                mbar_arrive_expect_tx(&ring_full[slot], kUnitBytes);
-                // x in 8-byte elements: a unit starts at uk * 16 blocks (a multiple of 16 bytes)
-                tma_load_2d(smem_addr(smem + static_cast<size_t>(slot) * kUnitBytes), &map,
-                            static_cast<int32_t>(uk * (kURB / 8u)), static_cast<int32_t>((tile_begin + t) * kTileRows),
-                            &ring_full[slot], policy);
-                issued = u + 1u;
+            const uint32_t sbase = smem_addr(smem);
+            uint32_t issued = 0, slot = 0, use = 0, t = 0, sk = 0;
+            for (uint32_t c = 0; c < copies; ++c) {
+                if (use > 0 && !wait_phase(&ring_empty[slot], (use - 1u) & 1u, abort_flag, a.status, 61u)) break;
+                mbar_arrive_expect_tx(&ring_full[slot], kSlotBytes);
+                // x in 8-byte elements: a slot starts at sk * 32 blocks (a multiple of 16 bytes)
+                tma_load_2d(sbase + slot * kSlotBytes, &map, static_cast<int32_t>(sk * (kSRB / 8u)),
+                            static_cast<int32_t>((tile_begin + t) * kTileRows), &ring_full[slot], policy);
+                issued = c + 1u;
+                if (++sk == spt) {
+                    sk = 0;
+                    ++t;
+                }
+                if (++slot == S) {
+                    slot = 0;
+                    ++use;
+                }
             }
             // every issued copy has landed before the CTA may exit
             const uint32_t first = issued > S ? issued - S : 0u;
@@ -355,13 +369,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             bool ok = wait_phase(table_full, 0, abort_flag, a.status, 63u);
             tc_fence_after();
             const uint32_t tbase = smem_addr(table);
+            uint32_t ab = 0, aph = 0, db = 0, dph = 0, uk = 0;
             for (uint32_t u = 0; u < total && ok; ++u) {
-                const uint32_t ab = u % kNA, db = u % kND;
-                ok = wait_phase(&a_full[ab], (u / kNA) & 1u, abort_flag, a.status, 64u);
-                if (ok && u >= kND) ok = wait_phase(&d_free[db], ((u / kND) - 1u) & 1u, abort_flag, a.status, 65u);
+                ok = wait_phase(&a_full[ab], aph, abort_flag, a.status, 64u);
+                if (ok && u >= kND) ok = wait_phase(&d_free[db], dph ^ 1u, abort_flag, a.status, 65u);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t uk = u % a.units;
 #pragma unroll
                 for (uint32_t sub = 0; sub < kUnitSteps; ++sub) {
                     const uint32_t s = uk * kUnitSteps + sub;
@@ -370,38 +383,47 @@ __global__ void __launch_bounds__(kThreads, 2)
                                   kmajor_desc(tbase + s * kStepTableBytes, 128u, 256u), idesc_i8<TYPE>());
                 }
                 tc_commit(&d_full[db]);
+                if (++uk == units) uk = 0;
+                if (++ab == kNA) {
+                    ab = 0;
+                    aph ^= 1u;
+                }
+                if (++db == kND) {
+                    db = 0;
+                    dph ^= 1u;
+                }
             }
             tc_commit(mma_done);  // arrives once every MMA issued above has completed
             mbar_wait_bounded(mma_done, 0, a.status, 66u);
         }
-    } else if (warp < 6) {
-        // ---------------- loaders ----------------
+    } else if (warp < 10) {
+        // ---------------- loaders: warp (quarter qd, K step sub) ----------------
         const uint32_t qd = warp & 3u;                  // TMEM lane quarter
+        const uint32_t sub = (warp - 2u) >> 2;          // which K step of each unit
         const uint32_t m = qd * 32u + lane;             // MMA row: 16 * phase + tile row
         const uint32_t p = m >> 4, r = m & 15u;
         bool ok = true;
+        uint32_t slot = 0, sph = 0, ab = 0, aph = 0, uk = 0;
         for (uint32_t u = 0; u < total && ok; ++u) {
-            const uint32_t slot = u % S, ab = u % kNA;
-            ok = wait_phase(&ring_full[slot], (u / S) & 1u, abort_flag, a.status, 67u);
-            if (ok && u >= kNA) ok = wait_phase(&a_free[ab], ((u / kNA) - 1u) & 1u, abort_flag, a.status, 68u);
+            const uint32_t half = uk & 1u;  // which unit of the slot
+            if (half == 0) ok = wait_phase(&ring_full[slot], sph, abort_flag, a.status, 67u);
+            if (ok && u >= kNA) ok = wait_phase(&a_free[ab], aph ^ 1u, abort_flag, a.status, 68u);
             if (!ok) break;
             tc_fence_after();  // the MMAs that read this A buffer have completed
-            const uint8_t* unit = smem + static_cast<size_t>(slot) * kUnitBytes + r * kPitch;
-            uint32_t av[16];
-            float dv[kUnitSteps];
-#pragma unroll
-            for (uint32_t sub = 0; sub < kUnitSteps; ++sub) {
+            if (uk * kUnitSteps + sub < a.steps) {
+                const uint8_t* row = smem + slot * kSlotBytes + r * kPitch + half * (kUnitBlocks * BB);
                 const uint32_t off = (sub * kPhases + p) * BB;  // this lane's block in the unit row
-                dv[sub] = half_bits_to_float(*reinterpret_cast<const uint16_t*>(unit + off));
+                const float dv = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + off));
                 const uint32_t qs = off + 2u;                  // first quant byte
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(unit + (qs & ~3u));
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(row + (qs & ~3u));
                 const uint32_t sh = (qs & 3u) * 8u;            // 0 or 16
+                uint32_t av[8];
                 if constexpr (TYPE == kQ8_0) {
                     uint32_t wv[9];
 #pragma unroll
                     for (uint32_t k = 0; k < 9; ++k) wv[k] = w[k];
 #pragma unroll
-                    for (uint32_t k = 0; k < 8; ++k) av[sub * 8u + k] = __funnelshift_r(wv[k], wv[k + 1], sh);
+                    for (uint32_t k = 0; k < 8; ++k) av[k] = __funnelshift_r(wv[k], wv[k + 1], sh);
                 } else {
                     uint32_t wv[5];
 #pragma unroll
@@ -409,45 +431,56 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                     for (uint32_t k = 0; k < 4; ++k) {
                         const uint32_t n = __funnelshift_r(wv[k], wv[k + 1], sh);
-                        av[sub * 8u + k] = n & 0x0F0F0F0Fu;             // elements 4k..4k+3: low nibbles
-                        av[sub * 8u + 4u + k] = (n >> 4) & 0x0F0F0F0Fu;  // elements 16+4k..: high nibbles
+                        av[k] = n & 0x0F0F0F0Fu;              // elements 4k..4k+3: low nibbles
+                        av[4u + k] = (n >> 4) & 0x0F0F0F0Fu;  // elements 16+4k..: high nibbles
                     }
                 }
+                tc_st_x8(tmem + kACol0 + ab * 16u + sub * 8u + ((qd * 32u) << 16), av);
+                sd[(ab * kUnitSteps + sub) * 128u + m] = dv;
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
-            tc_st_x16(tmem + kACol0 + ab * 16u + ((qd * 32u) << 16), av);
-#pragma unroll
-            for (uint32_t sub = 0; sub < kUnitSteps; ++sub) sd[(ab * kUnitSteps + sub) * 128u + m] = dv[sub];
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
+            const bool slot_done = half == 1u || uk + 1u == units;
             if (lane == 0) {
                 mbar_arrive(&ring_empty[slot]);
+                if (slot_done && half == 0u) mbar_arrive(&ring_empty[slot]);  // a slot of one unit
                 mbar_arrive(&a_full[ab]);
+            }
+            if (slot_done && ++slot == S) {
+                slot = 0;
+                sph ^= 1u;
+            }
+            if (++uk == units) uk = 0;
+            if (++ab == kNA) {
+                ab = 0;
+                aph ^= 1u;
             }
         }
     } else {
-        // ---------------- x table, then the epilogue ----------------
+        // ---------------- x table, then the epilogue: warp (quarter qd, K step sub) ----------------
         const uint32_t qd = warp & 3u;
-        const uint32_t et = threadIdx.x - 192u;  // 0..127
+        const uint32_t sub = (warp - 10u) >> 2;
+        const uint32_t et = threadIdx.x - 320u;  // 0..255
         grid_dependency_wait();                  // x may come from the previous kernel
         {
-            // 8 threads per block, 16 blocks per pass, up to 8 passes' loads in flight
+            // 8 threads per block, 32 blocks per pass, up to 4 passes' loads in flight
             const uint32_t q = et & 7u;
             const uint32_t nbt = a.steps * kPhases;  // a.nb rounded up to whole K steps (== a.nb)
             for (uint32_t base = 0; base < nbt; base += 128u) {
-                float4 v[8];
+                float4 v[4];
 #pragma unroll
-                for (uint32_t k = 0; k < 8; ++k) {
-                    const uint32_t b = base + k * 16u + (et >> 3);
+                for (uint32_t k = 0; k < 4; ++k) {
+                    const uint32_t b = base + k * 32u + (et >> 3);
                     v[k] = b < a.nb ? __ldg(reinterpret_cast<const float4*>(a.x + 32u * b + 4u * q))
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
-                for (uint32_t k = 0; k < 8; ++k) {
-                    const uint32_t b = base + k * 16u + (et >> 3);
+                for (uint32_t k = 0; k < 4; ++k) {
+                    const uint32_t b = base + k * 32u + (et >> 3);
                     // every lane runs the block code (its shuffles span the warp);
                     // blocks past the row store nothing
-                    if (base + k * 16u < nbt) limb_block<TYPE == kQ4_0>(v[k], b, q, b < nbt, table, consts);
+                    if (base + k * 32u < nbt) limb_block<TYPE == kQ4_0>(v[k], b, q, b < nbt, table, consts);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // table writes -> tensor-core reads
@@ -460,65 +493,71 @@ __global__ void __launch_bounds__(kThreads, 2)
         bool ok = true;
         float acc = 0.f;
         // every thread of the epilogue sees the table (its own warp group wrote it)
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, 256);
+        uint32_t ab = 0, aph = 0, db = 0, dph = 0, uk = 0, t = 0;
         for (uint32_t u = 0; u < total && ok; ++u) {
-            const uint32_t ab = u % kNA, db = u % kND;
-            ok = wait_phase(&d_full[db], (u / kND) & 1u, abort_flag, a.status, 69u);
+            ok = wait_phase(&d_full[db], dph, abort_flag, a.status, 69u);
             // the loaders' block scales of this unit (their arrival orders the sd stores)
-            ok = ok && wait_phase(&a_full[ab], (u / kNA) & 1u, abort_flag, a.status, 70u);
+            ok = ok && wait_phase(&a_full[ab], aph, abort_flag, a.status, 70u);
             if (!ok) break;
             tc_fence_after();
-            uint32_t v[kUnitSteps][8];
-#pragma unroll
-            for (uint32_t sub = 0; sub < kUnitSteps; ++sub)
-                tc_ld_x8(tmem + kDCol0 + db * (kUnitSteps * kN) + sub * kN + qd * 8u + ((qd * 32u) << 16), v[sub]);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            float dv[kUnitSteps];
-#pragma unroll
-            for (uint32_t sub = 0; sub < kUnitSteps; ++sub) dv[sub] = sd[(ab * kUnitSteps + sub) * 128u + m];
+            const uint32_t s = uk * kUnitSteps + sub;
+            uint32_t v[8];
+            float dv = 0.f;
+            if (s < a.steps) {
+                tc_ld_x8(tmem + kDCol0 + db * (kUnitSteps * kN) + sub * kN + qd * 8u + ((qd * 32u) << 16), v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                dv = sd[(ab * kUnitSteps + sub) * 128u + m];
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&d_free[db]);
                 mbar_arrive(&a_free[ab]);
             }
-            const uint32_t t = u / a.units, uk = u - t * a.units;
-#pragma unroll
-            for (uint32_t sub = 0; sub < kUnitSteps; ++sub) {
-                const uint32_t s = uk * kUnitSteps + sub;
-                if (s < a.steps) {
-                    const float4 c = consts[s * kPhases + p];
-                    const int d0 = static_cast<int>(hi ? v[sub][4] : v[sub][0]);
-                    const int d1 = static_cast<int>(hi ? v[sub][5] : v[sub][1]);
-                    const int d2 = static_cast<int>(hi ? v[sub][6] : v[sub][2]);
-                    const int d3 = static_cast<int>(hi ? v[sub][7] : v[sub][3]);
-                    const int vh = d0 * 128 + d1 - __float_as_int(c.z);
-                    const int vl = d2 * 128 + d3 - __float_as_int(c.w);
-                    acc = fmaf(static_cast<float>(vh), dv[sub] * c.x, acc);
-                    acc = fmaf(static_cast<float>(vl), dv[sub] * c.y, acc);
-                }
+            if (s < a.steps) {
+                const float4 c = consts[s * kPhases + p];
+                const int d0 = static_cast<int>(hi ? v[4] : v[0]);
+                const int d1 = static_cast<int>(hi ? v[5] : v[1]);
+                const int d2 = static_cast<int>(hi ? v[6] : v[2]);
+                const int d3 = static_cast<int>(hi ? v[7] : v[3]);
+                const int vh = d0 * 128 + d1 - __float_as_int(c.z);
+                const int vl = d2 * 128 + d3 - __float_as_int(c.w);
+                acc = fmaf(static_cast<float>(vh), dv * c.x, acc);
+                acc = fmaf(static_cast<float>(vl), dv * c.y, acc);
             }
-            if (uk + 1u == a.units) {
-                // tile done: add the 8 block phases of each row in phase order.  Two
-                // buffers by tile parity; a buffer is rewritten only after the sum of
-                // the tile two before has been read from it.
+            if (++ab == kNA) {
+                ab = 0;
+                aph ^= 1u;
+            }
+            if (++db == kND) {
+                db = 0;
+                dph ^= 1u;
+            }
+            if (++uk == units) {
+                uk = 0;
+                // tile done: add each row's 16 partial sums (8 block phases x 2 K-step
+                // warps) in a fixed order.  Two buffers by tile parity; a buffer is
+                // rewritten only after the sum of the tile two before was read from it.
                 const float pair = acc + __shfl_xor_sync(0xFFFFFFFFu, acc, 16);  // phases 2qd, 2qd+1
                 const uint32_t rbi = t & 1u;
-                float* rb = red + rbi * 64u;
+                float* rb = red + rbi * 128u;
                 if (t >= 2u && !wait_phase(&red_free[rbi], ((t >> 1) - 1u) & 1u, abort_flag, a.status, 71u)) {
                     ok = false;
                     break;
                 }
-                if (lane < 16) rb[qd * 16u + lane] = pair;
+                if (lane < 16) rb[(sub * 4u + qd) * 16u + lane] = pair;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&red_full[rbi]);
-                if (qd == 0) {
+                if (qd == 0 && sub == 0) {
                     if (!wait_phase(&red_full[rbi], (t >> 1) & 1u, abort_flag, a.status, 72u)) {
                         ok = false;
                         break;
                     }
                     if (lane < 16) {
-                        const float yv = ((rb[lane] + rb[16u + lane]) + rb[32u + lane]) + rb[48u + lane];
+                        float yv = 0.f;
+#pragma unroll
+                        for (uint32_t k = 0; k < 8; ++k) yv += rb[k * 16u + lane];
                         const uint32_t row = (tile_begin + t) * kTileRows + lane;
                         if (row < a.rows) a.y[row] = yv;
                     }
@@ -526,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     if (lane == 0) mbar_arrive(&red_free[rbi]);
                 }
                 acc = 0.f;
+                ++t;
             }
         }
     }
@@ -550,19 +590,21 @@ Tc8Plan plan_tc8(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int m
     const uint32_t nb = static_cast<uint32_t>(cols / 32u);
     const uint32_t steps = nb / kPhases;
     const uint32_t units = (steps + kUnitSteps - 1) / kUnitSteps;
-    // a unit row in shared memory: its 16 blocks plus 16 bytes, an odd multiple of
-    // 16 bytes, so the 16 rows of a loader read fall in different bank groups (the
-    // copy reads 16 bytes of the next unit, or zeros past the row end)
-    const uint32_t unit_bytes = kTileRows * (kUnitBlocks * bb + 16u);
+    // a ring slot (one copy) is 16 rows x 32 blocks; a row in shared memory is its
+    // blocks plus 16 bytes, an odd multiple of 16 bytes, so the 16 rows of a loader
+    // read fall in different bank groups (the copy reads 16 bytes of the next
+    // slot's blocks, or zeros past the row end)
+    const uint32_t unit_bytes = kTileRows * (kSlotUnits * kUnitBlocks * bb + 16u);
+    const uint32_t spt = (units + kSlotUnits - 1) / kSlotUnits;
     const uint64_t tiles = (rows + kTileRows - 1) / kTileRows;
     const uint64_t grid = tiles < static_cast<uint64_t>(num_sms) ? tiles : static_cast<uint64_t>(num_sms);
-    const uint64_t per_cta = (tiles + grid - 1) / grid * units;  // units of the busiest CTA
+    const uint64_t per_cta = (tiles + grid - 1) / grid * spt;  // copies of the busiest CTA
     // fixed part: x table, block constants, block scales, partial sums
     const uint32_t off_table_rel = 0;
     const uint32_t table = steps * kStepTableBytes;
     const uint32_t cbytes = steps * kPhases * 16u;
     const uint32_t sdb = kNA * kUnitSteps * 128u * 4u;
-    const uint32_t redb = 2u * 64u * 4u;
+    const uint32_t redb = 2u * 128u * 4u;
     auto smem_of = [&](uint32_t s) {
         const uint32_t bars = 8u * (2u * s + 2u * kNA + 2u * kND + 6u) + 16u;
         return s * unit_bytes + table + cbytes + sdb + redb + bars + off_table_rel;
