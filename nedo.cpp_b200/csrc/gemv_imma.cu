@@ -156,8 +156,17 @@ __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint
 // words of this thread's positions, the block exponent and the limb sums, all
 // written into the fragment-ordered pair table.  e_b makes max |x_b| * 2^e_b
 // fall in [2^26, 2^27).
+// A block holding a NaN or an infinity gets all-zero limbs and a NaN column
+// scale, so every row's result is NaN, as the reference's fp32 sums are for a
+// NaN (and, but for the sign of the infinities, for an infinite) element.
 template <bool SUMS>
 __device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, bool in, uint8_t* table) {
+    int bad = !(fabsf(v.x) <= 3.402823466e38f) || !(fabsf(v.y) <= 3.402823466e38f) ||
+              !(fabsf(v.z) <= 3.402823466e38f) || !(fabsf(v.w) <= 3.402823466e38f);
+    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 1);
+    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 2);
+    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 4);
+    if (bad) v = make_float4(0.f, 0.f, 0.f, 0.f);
     float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
@@ -219,7 +228,8 @@ __device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, boo
             // scale 2^(7*(2-la) - e) (in [2^-126, 2^115]: a normal float)
             const uint32_t la = 2u * q;
             int* te = reinterpret_cast<int*>(pe + 256u + (2u * odd + q) * 16u);
-            te[0] = static_cast<int>(static_cast<uint32_t>(7 * (2 - static_cast<int>(la)) - e + 127) << 23);
+            te[0] = bad ? static_cast<int>(0x7FC00000u)
+                        : static_cast<int>(static_cast<uint32_t>(7 * (2 - static_cast<int>(la)) - e + 127) << 23);
             te[1] = -8 * (q ? sum[2] : sum[0]);
             te[2] = -8 * (q ? sum[3] : sum[1]);
         }

@@ -234,3 +234,19 @@ def test_tensor_core_batch_worst_case_rounding(lib, cuda, oracle, t):
         lib.set_exact_batches(prev)
     for b in (0, batch - 1):
         assert_within_tol(exact[b], ref, absd, tol=TOL, what=f"exact mode token {b}")
+
+
+@pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
+@pytest.mark.parametrize("rows,cols,batch", [(300, 4096, 1), (11008, 4096, 1), (1000, 2048, 8), (1000, 4096, 64)])
+def test_nonfinite_activation_gives_nan(lib, cuda, t, rows, cols, batch):
+    # the reference's fp32 sums are NaN for every row when x holds a NaN
+    torch = cuda
+    w = B.gen_weight(t, rows, cols, 98)
+    x = B.gen_x(cols, 98, batch=batch)
+    x[:, cols // 3] = np.nan
+    wd, xd = torch.from_numpy(w).cuda(), torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    yd = torch.zeros((batch, rows), device="cuda")
+    lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd.data_ptr(), yd.data_ptr(), batch, _s(torch))
+    torch.cuda.synchronize()
+    lib.status()
+    assert np.all(np.isnan(yd.cpu().numpy()))

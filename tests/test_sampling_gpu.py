@@ -77,8 +77,17 @@ def test_lm_head_host_entry_points(lib, cuda, t, rows, cols):
         exp = _expected_topk(logits, k)
         assert np.array_equal(ids.astype(np.int64), exp)
         assert np.array_equal(vals.view(np.uint32), logits[exp].view(np.uint32))
+    # the greedy pick runs the matvec with the argmax fused (for Q8_0 / Q4_0 another
+    # kernel than the plain matvec, so its logits may differ in the last bits):
+    # bit-exact against the same fused launch on device buffers
     idx, val = lib.lm_head_argmax(t, rows, cols, w, x)
-    assert idx == int(np.argmax(logits)) and val == logits[idx]
+    ya = torch.empty(rows, device="cuda")
+    ia = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    lib.matvec_argmax_dev(t, rows, cols, wd.data_ptr(), xd.data_ptr(), ya.data_ptr(), ia.data_ptr())
+    torch.cuda.synchronize()
+    fused = ya.cpu().numpy()
+    assert idx == int(ia.item()) == int(np.argmax(fused)) and val == fused[idx]
+    assert idx == int(np.argmax(logits))  # both logit vectors pick the same token here
     lib.weight_evict(w)
 
 
