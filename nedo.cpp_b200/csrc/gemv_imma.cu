@@ -49,7 +49,13 @@
 // weight as soon as the previous kernel's CTA on its SM exits, and reads x only
 // after that kernel has completed.  Every wait is bounded; a CTA-wide abort
 // flag stops every warp after the first timed-out wait.
+//
+// One token vector whose CTA share fits in shared memory (the 25 MB-class
+// matrices and smaller) runs gemv_imma_slice_kernel instead (see there): no
+// ring, wide copy units, and finer work items that share each x-side read
+// among all of a CTA's tiles.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "launch.h"
@@ -80,6 +86,7 @@ struct ImmaArgs {
     uint32_t team;         // warps sharing a tile (a power of two dividing warps)
     uint32_t slots;
     uint32_t unit_bytes;   // 16 * box_bytes
+    uint32_t early_chunks; // slice: chunks copied before x is requested
     uint64_t ldx;          // floats between token vectors of x
     uint64_t ldy;          // floats between token vectors of y
     DeviceStatus* status;
@@ -136,6 +143,37 @@ struct Pair<kQ4_0> {
     static constexpr uint32_t kBytes = 36, kBlock = 18;
 };
 
+// Q4_0: the start value of each lane's low-limb D column carries 1.5 * 2^23 as
+// float bits (0x4B400000), so the combined integer 128 * d_hi + d_lo of a
+// block (|value| < 2^22) is directly the bit pattern of 1.5 * 2^23 + value and
+// one FADD turns it into the exact float (no integer-to-float conversion).
+constexpr int kQ4Magic = 0x4B400000;
+constexpr float kQ4MagicF = 12582912.0f;  // 1.5 * 2^23
+
+// d = A * B + c (int8 inputs, exact int32 accumulation); A unsigned for Q4_0 nibbles.
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void imma_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1, int c0, int c1, int c2, int c3) {
+    if (A_UNSIGNED)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+// The float value of a combined block dot (for Q4_0 exact, through the offset
+// carried in the start value; for Q8_0 the conversion's rounding).
+template <uint32_t TYPE>
+__device__ __forceinline__ float dot_value(int v) {
+    if constexpr (TYPE == kQ4_0) return __int_as_float(v) - kQ4MagicF;
+    else return static_cast<float>(v);
+}
+
 // d += A * B (int8 inputs, exact int32 accumulation); A unsigned for Q4_0 nibbles.
 template <bool A_UNSIGNED>
 __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -152,88 +190,120 @@ __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// One 32-element block of x, 8 threads (4 positions each): the four limb
-// words of this thread's positions, the block exponent and the limb sums, all
-// written into the fragment-ordered pair table.  e_b makes max |x_b| * 2^e_b
-// fall in [2^26, 2^27).
+// N 32-element blocks of x per thread group, 8 threads per block (4 positions
+// each): the four limb words of this thread's positions, the block exponent and
+// the limb sums, all written into the fragment-ordered pair table.  The N
+// blocks are processed in lockstep so that their shuffles overlap.  e_b makes
+// max |x_b| * 2^e_b fall in [2^26, 2^27).
 // A block holding a NaN or an infinity gets all-zero limbs and a NaN column
 // scale, so every row's result is NaN, as the reference's fp32 sums are for a
 // NaN (and, but for the sign of the infinities, for an infinite) element.
-template <bool SUMS>
-__device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, bool in, uint8_t* table) {
-    int bad = !(fabsf(v.x) <= 3.402823466e38f) || !(fabsf(v.y) <= 3.402823466e38f) ||
-              !(fabsf(v.z) <= 3.402823466e38f) || !(fabsf(v.w) <= 3.402823466e38f);
-    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 1);
-    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 2);
-    bad |= __shfl_xor_sync(0xFFFFFFFFu, bad, 4);
-    if (bad) v = make_float4(0.f, 0.f, 0.f, 0.f);
-    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-    int e = 0;  // an all-zero block keeps e = 0 (all limbs 0)
-    if (m > 0.f) {
-        const int E = static_cast<int>((__float_as_uint(m) >> 23) & 0xFFu) - 127;  // m in [2^E, 2^(E+1))
-        e = 26 - E;                                                                 // in [-101, 153]
-        if (e > 126) e = 126;
+template <bool SUMS, uint32_t N>
+__device__ __forceinline__ void limb_blocks(const float4 (&vin)[N], const uint32_t (&b)[N], uint32_t q,
+                                            const bool (&in)[N], uint8_t* table) {
+    // |v| as bits: the order of finite magnitudes, NaN and infinity at 0x7F800000 and above
+    uint32_t mb[N];
+#pragma unroll
+    for (uint32_t n = 0; n < N; ++n)
+        mb[n] = max(max(__float_as_uint(vin[n].x) & 0x7FFFFFFFu, __float_as_uint(vin[n].y) & 0x7FFFFFFFu),
+                    max(__float_as_uint(vin[n].z) & 0x7FFFFFFFu, __float_as_uint(vin[n].w) & 0x7FFFFFFFu));
+#pragma unroll
+    for (uint32_t k = 1; k < 8; k <<= 1)
+#pragma unroll
+        for (uint32_t n = 0; n < N; ++n) mb[n] = max(mb[n], __shfl_xor_sync(0xFFFFFFFFu, mb[n], k));
+    uint32_t L[N][4];
+    int sum[N][4];
+    bool bad[N];
+    int e[N];
+#pragma unroll
+    for (uint32_t n = 0; n < N; ++n) {
+        bad[n] = mb[n] >= 0x7F800000u;
+        const float4 v = bad[n] ? make_float4(0.f, 0.f, 0.f, 0.f) : vin[n];
+        e[n] = 0;  // an all-zero block keeps e = 0 (all limbs 0)
+        if (!bad[n] && mb[n] != 0u) {
+            const int E = static_cast<int>(mb[n] >> 23) - 127;  // max |x_b| in [2^E, 2^(E+1))
+            int en = 26 - E;                                     // in [-101, 153]
+            if (en > 126) en = 126;
+            e[n] = en;
+        }
+        const float sc = __uint_as_float(static_cast<uint32_t>(e[n] + 127) << 23);  // 2^e, exact
+        // |X| <= 2^27 - 8 (a float below 2^27 scaled by a power of two is an integer
+        // multiple of 8 there), so X = L0*2^21 + L1*2^14 + L2*2^7 + L3 with
+        // L0 = X >> 21 in [-64, 63] and L1..L3 = the 7-bit floor remainders in [0, 127].
+        // Limb l of element i is byte (3 - l) of X << (3 - l), masked to 7 bits for
+        // l > 0; PRMT gathers that byte of the four elements into one word.
+        const uint32_t X0 = static_cast<uint32_t>(__float2int_rn(v.x * sc));
+        const uint32_t X1 = static_cast<uint32_t>(__float2int_rn(v.y * sc));
+        const uint32_t X2 = static_cast<uint32_t>(__float2int_rn(v.z * sc));
+        const uint32_t X3 = static_cast<uint32_t>(__float2int_rn(v.w * sc));
+        // byte k of a and of b -> bytes 0, 1 (selector 0x33..: the upper two bytes are don't-care)
+        auto gather = [](uint32_t a, uint32_t bb, uint32_t c, uint32_t d, uint32_t sel) {
+            return prmt(prmt(a, bb, sel), prmt(c, d, sel), 0x5410u);
+        };
+        L[n][3] = gather(X0, X1, X2, X3, 0x3340u) & 0x7F7F7F7Fu;
+        L[n][2] = gather(X0 << 1, X1 << 1, X2 << 1, X3 << 1, 0x3351u) & 0x7F7F7F7Fu;
+        L[n][1] = gather(X0 << 2, X1 << 2, X2 << 2, X3 << 2, 0x3362u) & 0x7F7F7F7Fu;
+        L[n][0] = gather(X0 << 3, X1 << 3, X2 << 3, X3 << 3, 0x3373u);
+        sum[n][0] = sum[n][1] = sum[n][2] = sum[n][3] = 0;
     }
-    const float sc = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);  // 2^e, exact
-    // |X| <= 2^27 - 8 (a float below 2^27 scaled by a power of two is an integer
-    // multiple of 8 there), so X = L0*2^21 + L1*2^14 + L2*2^7 + L3 with
-    // L0 = X >> 21 in [-64, 63] and L1..L3 = the 7-bit floor remainders in [0, 127].
-    // Limb l of element i is byte (3 - l) of X << (3 - l), masked to 7 bits for
-    // l > 0; PRMT gathers that byte of the four elements into one word.
-    const uint32_t X0 = static_cast<uint32_t>(__float2int_rn(v.x * sc));
-    const uint32_t X1 = static_cast<uint32_t>(__float2int_rn(v.y * sc));
-    const uint32_t X2 = static_cast<uint32_t>(__float2int_rn(v.z * sc));
-    const uint32_t X3 = static_cast<uint32_t>(__float2int_rn(v.w * sc));
-    // byte k of a and of b -> bytes 0, 1 (selector 0x33..: the upper two bytes are don't-care)
-    auto gather = [](uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t sel) {
-        return prmt(prmt(a, b, sel), prmt(c, d, sel), 0x5410u);
-    };
-    uint32_t L[4];
-    L[3] = gather(X0, X1, X2, X3, 0x3340u) & 0x7F7F7F7Fu;
-    L[2] = gather(X0 << 1, X1 << 1, X2 << 1, X3 << 1, 0x3351u) & 0x7F7F7F7Fu;
-    L[1] = gather(X0 << 2, X1 << 2, X2 << 2, X3 << 2, 0x3362u) & 0x7F7F7F7Fu;
-    L[0] = gather(X0 << 3, X1 << 3, X2 << 3, X3 << 3, 0x3373u);
-    int sum[4] = {0, 0, 0, 0};  // limb sums over the block (Q4_0 start values only)
     if (SUMS) {
-        // two sums per word: low 16 bits a non-negative sum (<= 32 * 127), high 16 bits the other
-        int s32 = __dp4a(static_cast<int>(L[3]), 0x01010101, 0) + __dp4a(static_cast<int>(L[0]), 0x01010101, 0) * 65536;
-        int s21 = __dp4a(static_cast<int>(L[2]), 0x01010101, 0) + __dp4a(static_cast<int>(L[1]), 0x01010101, 0) * 65536;
-        s32 += __shfl_xor_sync(0xFFFFFFFFu, s32, 1);
-        s21 += __shfl_xor_sync(0xFFFFFFFFu, s21, 1);
-        s32 += __shfl_xor_sync(0xFFFFFFFFu, s32, 2);
-        s21 += __shfl_xor_sync(0xFFFFFFFFu, s21, 2);
-        s32 += __shfl_xor_sync(0xFFFFFFFFu, s32, 4);
-        s21 += __shfl_xor_sync(0xFFFFFFFFu, s21, 4);
-        sum[3] = s32 & 0xFFFF;
-        sum[0] = (s32 - sum[3]) >> 16;
-        sum[2] = s21 & 0xFFFF;
-        sum[1] = (s21 - sum[2]) >> 16;
+        // limb sums over the block (Q4_0 start values), two per word: low 16 bits a
+        // non-negative sum (<= 32 * 127), high 16 bits the other
+        int s32[N], s21[N];
+#pragma unroll
+        for (uint32_t n = 0; n < N; ++n) {
+            s32[n] = __dp4a(static_cast<int>(L[n][3]), 0x01010101, 0) +
+                     __dp4a(static_cast<int>(L[n][0]), 0x01010101, 0) * 65536;
+            s21[n] = __dp4a(static_cast<int>(L[n][2]), 0x01010101, 0) +
+                     __dp4a(static_cast<int>(L[n][1]), 0x01010101, 0) * 65536;
+        }
+#pragma unroll
+        for (uint32_t k = 1; k < 8; k <<= 1)
+#pragma unroll
+            for (uint32_t n = 0; n < N; ++n) {
+                s32[n] += __shfl_xor_sync(0xFFFFFFFFu, s32[n], k);
+                s21[n] += __shfl_xor_sync(0xFFFFFFFFu, s21[n], k);
+            }
+#pragma unroll
+        for (uint32_t n = 0; n < N; ++n) {
+            sum[n][3] = s32[n] & 0xFFFF;
+            sum[n][0] = (s32[n] - sum[n][3]) >> 16;
+            sum[n][2] = s21[n] & 0xFFFF;
+            sum[n][1] = (s21[n] - sum[n][2]) >> 16;
+        }
     }
-    if (in) {
+#pragma unroll
+    for (uint32_t n = 0; n < N; ++n) {
+        if (!in[n]) continue;
         // lane (g, t) of the pair's IMMAs takes limb g & 3 of block (g >= 4 ? odd : even),
         // positions 4t.. (w_lo) and 16+4t.. (w_hi): this thread's word is w_lo of
         // t = q (q < 4) or w_hi of t = q - 4
-        const uint32_t odd = b & 1u;
-        uint8_t* pe = table + static_cast<size_t>(b >> 1) * kPairTableBytes;
+        const uint32_t odd = b[n] & 1u;
+        uint8_t* pe = table + static_cast<size_t>(b[n] >> 1) * kPairTableBytes;
 #pragma unroll
         for (uint32_t l = 0; l < 4; ++l) {
             const uint32_t lane = (4u * odd + l) * 4u + (q & 3u);
-            reinterpret_cast<uint32_t*>(pe + lane * 8u)[q >> 2] = L[l];
+            reinterpret_cast<uint32_t*>(pe + lane * 8u)[q >> 2] = L[n][l];
         }
         if (q < 2) {
             // t = 2*odd + q: D columns 2t, 2t+1 = limbs la = 2q and la+1 of this block,
             // scale 2^(7*(2-la) - e) (in [2^-126, 2^115]: a normal float)
             const uint32_t la = 2u * q;
             int* te = reinterpret_cast<int*>(pe + 256u + (2u * odd + q) * 16u);
-            te[0] = bad ? static_cast<int>(0x7FC00000u)
-                        : static_cast<int>(static_cast<uint32_t>(7 * (2 - static_cast<int>(la)) - e + 127) << 23);
-            te[1] = -8 * (q ? sum[2] : sum[0]);
-            te[2] = -8 * (q ? sum[3] : sum[1]);
+            te[0] = bad[n] ? static_cast<int>(0x7FC00000u)
+                           : static_cast<int>(static_cast<uint32_t>(7 * (2 - static_cast<int>(la)) - e[n] + 127) << 23);
+            te[1] = -8 * (q ? sum[n][2] : sum[n][0]);
+            te[2] = -8 * (q ? sum[n][3] : sum[n][1]) + (SUMS ? kQ4Magic : 0);
         }
     }
+}
+
+template <bool SUMS>
+__device__ __forceinline__ void limb_block(float4 v, uint32_t b, uint32_t q, bool in, uint8_t* table) {
+    const float4 vv[1] = {v};
+    const uint32_t bb[1] = {b};
+    const bool ii[1] = {in};
+    limb_blocks<SUMS, 1>(vv, bb, q, ii, table);
 }
 
 // All consumer threads: build the tables of blocks [0, nblocks) of `ntok`
@@ -336,17 +406,15 @@ __device__ __forceinline__ void segment_dot(const uint8_t* r0p, const uint8_t* r
                 imma<false>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
             } else {
                 // accumulators start at -8 * sum L of their column (the nibble offset)
-                d[0] = d[2] = te.y;
-                d[1] = d[3] = te.z;
-                imma<true>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo);
+                imma_c<true>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo, te.y, te.z, te.y, te.z);
                 imma<true>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
             }
             // d[0], d[1]: row g, limbs (2(t&1), 2(t&1)+1) of block (t>>1); d[2], d[3]: row g+8
             const float xs = __int_as_float(te.x);
             const int v0 = d[0] * 128 + d[1];
             const int v1 = d[2] * 128 + d[3];
-            acc0[k] = fmaf(static_cast<float>(v0), d0 * xs, acc0[k]);
-            acc1[k] = fmaf(static_cast<float>(v1), d1 * xs, acc1[k]);
+            acc0[k] = fmaf(dot_value<TYPE>(v0), d0 * xs, acc0[k]);
+            acc1[k] = fmaf(dot_value<TYPE>(v1), d1 * xs, acc1[k]);
         }
     }
 }
@@ -568,6 +636,308 @@ __global__ void __maxnreg__(NT == 1 ? 96 : 128)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Resident-slice variant (one token vector, whole rows in one column group).
+// A CTA's whole share of the weight fits in its shared memory, so every copy
+// unit has its own slot and barrier and nothing is ever waited on for reuse.
+//
+// Streaming.  Copy units are wide (16 rows x UP block pairs, about 1.1 KB per
+// row): the tensor-map engine's cost grows with the number of box rows, and
+// units this wide stream a 25 MB matrix at the HBM rate where 0.5 KB rows do
+// not.  At CTA start (before griddepcontrol.wait) the producer asks L2 to
+// prefetch the whole slice; the copies into shared memory are issued only
+// after every consumer warp has issued its loads of x, so that x (needed first)
+// is not queued behind this SM's weight stream.  Copies go out chunk-major
+// (chunk 0 of every tile first), the order the compute consumes them.
+//
+// Compute.  A work item is one sub-segment of kSubPairs block pairs of up to R
+// consecutive tiles: the x side of each pair (B registers, column scales,
+// start values) is read from the table once and applied to every tile, which
+// cuts the shared-memory traffic per tile-pair by about a third.  Items are
+// dealt round-robin to the consumer warps in landing order.  Every item folds
+// its per-tile row sums into its own slot [tile][sub-segment]; after all warps
+// are done each tile's rows are added over its sub-segments in order, so the
+// result depends only on the shape, never on timing.
+constexpr uint32_t kSubPairs = 4;
+constexpr uint64_t kEarlyBytes = 160u * 1024u;  // weight bytes a CTA copies before requesting x
+
+// One block pair of one 16-row tile (rows g, g+8 at p0 / p1) against the x side
+// already in registers: the two IMMAs and the per-block recombination.
+template <uint32_t TYPE>
+__device__ __forceinline__ void pair_tile_dot(const uint8_t* p0, const uint8_t* p1, uint32_t t, uint32_t b0lo,
+                                              uint32_t b1lo, uint32_t b0hi, uint32_t b1hi, const int4& te, float& acc0,
+                                              float& acc1) {
+    const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;
+    uint32_t A[2][4];
+    if constexpr (TYPE == kQ8_0) {
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+            const uint32_t o = 16u * h + 4u * t;
+            const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + o);
+            const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + o);
+            A[h][0] = __funnelshift_r(e0[0], e0[1], 16);
+            A[h][1] = __funnelshift_r(e1[0], e1[1], 16);
+            A[h][2] = *reinterpret_cast<const uint32_t*>(p0 + 36u + o);
+            A[h][3] = *reinterpret_cast<const uint32_t*>(p1 + 36u + o);
+        }
+    } else {
+        const uint32_t* e0 = reinterpret_cast<const uint32_t*>(p0 + 4u * t);
+        const uint32_t* e1 = reinterpret_cast<const uint32_t*>(p1 + 4u * t);
+        const uint32_t w0 = __funnelshift_r(e0[0], e0[1], 16);
+        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(p0 + 20u + 4u * t);
+        const uint32_t w1 = __funnelshift_r(e1[0], e1[1], 16);
+        const uint32_t w3 = *reinterpret_cast<const uint32_t*>(p1 + 20u + 4u * t);
+        const uint32_t m = 0x0F0F0F0Fu;
+        A[0][0] = w0 & m;
+        A[0][1] = w1 & m;
+        A[0][2] = w2 & m;
+        A[0][3] = w3 & m;
+        A[1][0] = (w0 >> 4) & m;
+        A[1][1] = (w1 >> 4) & m;
+        A[1][2] = (w2 >> 4) & m;
+        A[1][3] = (w3 >> 4) & m;
+    }
+    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk));
+    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk));
+    int d[4];
+    if constexpr (TYPE == kQ8_0) {
+        imma_c<false>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo, 0, 0, 0, 0);
+        imma<false>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
+    } else {
+        imma_c<true>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo, te.y, te.z, te.y, te.z);
+        imma<true>(d, A[1][0], A[1][1], A[1][2], A[1][3], b0hi, b1hi);
+    }
+    const float xs = __int_as_float(te.x);
+    const int v0 = d[0] * 128 + d[1];
+    const int v1 = d[2] * 128 + d[3];
+    acc0 = fmaf(dot_value<TYPE>(v0), d0 * xs, acc0);
+    acc1 = fmaf(dot_value<TYPE>(v1), d1 * xs, acc1);
+}
+
+// One work item: `valid` (<= kSubPairs) block pairs of nt <= R tiles whose rows
+// g / g+8 sit at r0 / r1 + r * tstep (independent work for the schedulers).
+template <uint32_t TYPE, uint32_t R>
+__device__ __forceinline__ void item_dot(const uint8_t* r0, const uint8_t* r1, size_t tstep, uint32_t nt,
+                                         const uint8_t* pt, uint32_t valid, uint32_t lane, uint32_t even_mask,
+                                         float (&acc0)[R], float (&acc1)[R]) {
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    const uint32_t t = lane & 3u;
+#pragma unroll
+    for (uint32_t p = 0; p < kSubPairs; ++p) {
+        if (p >= valid) break;
+        const uint8_t* ptk = pt + p * kPairTableBytes;
+        const uint2 w = *reinterpret_cast<const uint2*>(ptk + lane * 8u);
+        const int4 te = *reinterpret_cast<const int4*>(ptk + 256u + t * 16u);
+        const uint32_t b0lo = w.x & even_mask, b1lo = w.x & ~even_mask;
+        const uint32_t b0hi = w.y & even_mask, b1hi = w.y & ~even_mask;
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r) {
+            if (r < nt)
+                pair_tile_dot<TYPE>(r0 + r * tstep + p * pb, r1 + r * tstep + p * pb, t, b0lo, b1lo, b0hi, b1hi, te,
+                                    acc0[r], acc1[r]);
+        }
+    }
+}
+
+template <uint32_t TYPE, uint32_t UP, uint32_t R>
+__global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ CUtensorMap map, const ImmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t W = a.warps;
+    const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * blockIdx.x / gridDim.x);
+    const uint32_t tile_end = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t my_tiles = tile_end - tile_begin;
+    const uint32_t nchunk = (a.pairs_total + UP - 1u) / UP;
+    const uint32_t nunits = my_tiles * nchunk;
+    const uint32_t nsub = (a.pairs_total + kSubPairs - 1u) / kSubPairs;  // sub-segments per tile
+    const uint32_t tiles_cap = a.slots / nchunk;
+    // [units: slots x unit_bytes, unit (t, c) at t * nchunk + c][pair table]
+    // [partial sums: tiles_cap x nsub x 16][full: slots][x requested][abort flag]
+    uint8_t* table = smem + static_cast<size_t>(a.slots) * a.unit_bytes;
+    float* part = reinterpret_cast<float*>(table + static_cast<size_t>(a.group_pairs) * kPairTableBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(part + static_cast<size_t>(tiles_cap) * nsub * 16u);
+    uint64_t* xbar = full + a.slots;
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(xbar + 1);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t u = 0; u < nunits; ++u) mbar_init(&full[u], 1);
+        mbar_init(xbar, W);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    __syncwarp();
+    __syncthreads();
+    grid_launch_dependents();
+
+    if (warp == W) {
+        // producer (one thread)
+        if (lane != 0) return;
+        const uint64_t policy = l2_policy_evict_first();
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t c = 0; c < nchunk && ok; ++c) {
+            // the first early_chunks chunks stream during griddepcontrol.wait; the rest
+            // once every consumer warp has issued its x loads
+            if (c == a.early_chunks) ok = mbar_wait_bounded(xbar, 0u, a.status, 24u);
+            if (!ok) break;
+            for (uint32_t t = 0; t < my_tiles; ++t, ++issued) {
+                const uint32_t u = t * nchunk + c;
+                mbar_arrive_expect_tx(&full[u], a.unit_bytes);
+                // x in 8-byte elements: UP pairs are a multiple of 32 bytes
+                tma_load_2d_hint(smem_addr(smem + static_cast<size_t>(u) * a.unit_bytes), &map,
+                                 static_cast<int32_t>(c * UP * pb / 8u),
+                                 static_cast<int32_t>((tile_begin + t) * kTileRows), &full[u], policy);
+            }
+        }
+        if (!ok) *abort_flag = 1u;
+        // every issued copy lands before the CTA may exit
+        for (uint32_t c = 0, k = 0; c < nchunk; ++c)
+            for (uint32_t t = 0; t < my_tiles && k < issued; ++t, ++k)
+                mbar_wait_bounded(&full[t * nchunk + c], 0u, a.status, 22u);
+        return;
+    }
+
+    constexpr bool kQ4 = TYPE == kQ4_0;
+    const uint32_t g = lane >> 2;
+    const uint32_t even_mask = g < 4 ? 0xFFFFFFFFu : 0u;
+    const size_t off_a = static_cast<size_t>(g) * a.box_bytes;
+    const size_t off_b = off_a + 8u * static_cast<size_t>(a.box_bytes);
+
+    grid_dependency_wait();  // x may come from the previous kernel
+    {
+        // the x limb table: every x load issued, the producer released, then the limbs
+        const uint32_t tid = threadIdx.x, per_pass = W * 32u / 8u, q = tid & 7u;
+        const uint32_t blocks = 2u * a.pairs_total;  // at most per_pass * kLimbPasses (planned)
+        float4 v[kLimbPasses];
+#pragma unroll
+        for (uint32_t k = 0; k < kLimbPasses; ++k) {
+            const uint32_t f = k * per_pass + tid / 8u;
+            v[k] = f < blocks ? __ldg(reinterpret_cast<const float4*>(a.x + 32u * f + 4u * q))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+#pragma unroll
+        for (uint32_t k = 0; k < kLimbPasses; k += 2) {
+            // the 8 threads of a block share f (the shuffles inside span exactly them)
+            if (k * per_pass >= blocks) break;
+            const uint32_t f0 = k * per_pass + tid / 8u, f1 = f0 + per_pass;
+            const float4 vv[2] = {v[k], v[k + 1]};
+            const uint32_t bb[2] = {f0, f1};
+            const bool ii[2] = {f0 < blocks, f1 < blocks};
+            limb_blocks<kQ4, 2>(vv, bb, q, ii, table);
+        }
+    }
+    named_barrier_sync(1, W * 32u);
+
+    const uint32_t ngroups = (my_tiles + R - 1u) / R;
+    const uint32_t items = nsub * ngroups;
+    const size_t tstep = static_cast<size_t>(nchunk) * a.unit_bytes;  // unit (t + 1, c) - unit (t, c)
+    bool ok = true;
+    for (uint32_t i = warp; i < items; i += W) {
+        const uint32_t s = i / ngroups, grp = i - s * ngroups;
+        const uint32_t t0 = grp * R, nt = my_tiles - t0 < R ? my_tiles - t0 : R;
+        const uint32_t p0 = s * kSubPairs, c = p0 / UP;
+        if (ok && *abort_flag != 0u) ok = false;
+        for (uint32_t r = 0; r < nt && ok; ++r)
+            if (!mbar_wait_bounded(&full[(t0 + r) * nchunk + c], 0u, a.status, 23u)) {
+                ok = false;
+                *abort_flag = 1u;
+            }
+        if (!ok) continue;
+        const uint8_t* unit = smem + static_cast<size_t>(t0 * nchunk + c) * a.unit_bytes +
+                              static_cast<size_t>(p0 - c * UP) * pb;
+        const uint8_t* pt = table + static_cast<size_t>(p0) * kPairTableBytes;
+        float acc0[R], acc1[R];
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r) acc0[r] = acc1[r] = 0.f;
+        const uint32_t left = a.pairs_total - p0;
+        item_dot<TYPE, R>(unit + off_a, unit + off_b, tstep, nt, pt, left < kSubPairs ? left : kSubPairs, lane,
+                          even_mask, acc0, acc1);
+        // fold the four t-lanes of each row: row r of a tile is acc0 (r < 8) or acc1
+        // (r >= 8) of lane 4 (r mod 8); lane r stores it in the item's slot
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r) {
+            float c0 = acc0[r], c1 = acc1[r];
+            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
+            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
+            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
+            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
+            const uint32_t rr = lane & 15u;
+            const float v0 = __shfl_sync(0xFFFFFFFFu, c0, 4u * (rr & 7u));
+            const float v1 = __shfl_sync(0xFFFFFFFFu, c1, 4u * (rr & 7u));
+            if (r < nt && lane < 16)
+                part[(static_cast<size_t>(t0 + r) * nsub + s) * 16u + lane] = rr < 8 ? v0 : v1;
+        }
+    }
+    named_barrier_sync(1, W * 32u);
+    const bool aborted = *abort_flag != 0u;
+    if (!aborted) {
+        for (uint32_t t = warp; t < my_tiles; t += W) {
+            if (lane < 16) {
+                float sum = 0.f;
+                for (uint32_t s = 0; s < nsub; ++s) sum += part[(static_cast<size_t>(t) * nsub + s) * 16u + lane];
+                const uint64_t row = static_cast<uint64_t>(tile_begin + t) * kTileRows + lane;
+                if (row < a.rows) {
+                    a.y[row] = sum;
+                    for (uint32_t q = 0; q < a.npeers; ++q) a.peer_y[q][a.peer_row_offset + row] = sum;
+                }
+            }
+        }
+    }
+    if (a.npeers != 0u) {
+        // every warp's peer stores are visible system-wide before the CTA is
+        // published on each peer with a release add
+        __threadfence_system();
+        named_barrier_sync(1, W * 32u);
+        if (warp == 0 && lane == 0 && !aborted)
+            for (uint32_t k = 0; k < a.npeers; ++k)
+                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_signal[k]) : "memory");
+    }
+}
+
+template <uint32_t TYPE, uint32_t UP, uint32_t R>
+cudaError_t launch_slice_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                           bool pdl) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_imma_slice_kernel<TYPE, UP, R>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3((plan.warps + 1) * 32);
+    cfg.dynamicSmemBytes = plan.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_imma_slice_kernel<TYPE, UP, R>, map, args);
+}
+
+template <uint32_t TYPE>
+cudaError_t launch_slice_p(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                           bool pdl) {
+    // tiles sharing one x-side read: all of a CTA's tiles up to 5, else 2
+    const bool wide = plan.tile_group > 2;
+    switch (plan.seg_pairs) {
+        case 8: return wide ? launch_slice_t<TYPE, 8, 5>(plan, map, args, stream, pdl)
+                            : launch_slice_t<TYPE, 8, 2>(plan, map, args, stream, pdl);
+        case 16: return wide ? launch_slice_t<TYPE, 16, 5>(plan, map, args, stream, pdl)
+                             : launch_slice_t<TYPE, 16, 2>(plan, map, args, stream, pdl);
+        case 32: return wide ? launch_slice_t<TYPE, 32, 5>(plan, map, args, stream, pdl)
+                             : launch_slice_t<TYPE, 32, 2>(plan, map, args, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 template <uint32_t TYPE, uint32_t SEG, bool MULTI, uint32_t NT>
 cudaError_t launch_imma_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
                           bool pdl) {
@@ -624,6 +994,15 @@ cudaError_t launch_imma_p(const ImmaPlan& plan, const CUtensorMap& map, const Im
 
 uint64_t align_up64(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
+// NEDO_GPU_IMMA_SLICE=0 keeps one-token launches on the ring kernel (for comparisons).
+bool slice_allowed() {
+    static const bool allowed = [] {
+        const char* e = getenv("NEDO_GPU_IMMA_SLICE");
+        return !(e && e[0] == '0');
+    }();
+    return allowed;
+}
+
 // Bytes of one box row of `bp` block pairs: the data rounded to an odd
 // multiple of 16 bytes (the eight fragment rows of a load then fall in
 // distinct 16-byte bank groups).
@@ -655,6 +1034,47 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     const uint64_t per_sm = t.ctas_per_sm ? t.ctas_per_sm : 1u;
     const uint64_t grid = tiles < per_sm * num_sms ? tiles : per_sm * num_sms;
     const uint64_t tiles_per_cta = (tiles + grid - 1) / grid;
+    if (tokens == 1 && t.slice != 0 && slice_allowed() && wide && per_sm == 1) {
+        // resident slice: wide units (Q4_0 32 pairs = 1152 B, Q8_0 16 pairs = 1088 B
+        // per row), narrower when the row is shorter
+        uint64_t up = type == kQ4_0 ? 32u : 16u;
+        while (up > 8u && up / 2u >= pairs_total) up /= 2u;
+        const uint64_t box = box_row_bytes(up, pair_bytes);
+        const uint64_t nchunk = (pairs_total + up - 1) / up;
+        const uint64_t slots = tiles_per_cta * nchunk;
+        const uint64_t unit = kTileRows * box;
+        const uint64_t nsub = (pairs_total + kSubPairs - 1) / kSubPairs;
+        const uint64_t smem = slots * unit + pairs_total * kPairTableBytes + tiles_per_cta * nsub * 64u + 8u * slots + 32u;
+        // the x table's blocks in one pass of the consumer threads' registers
+        if (box <= kMaxBoxBytes && smem <= budget && 2u * pairs_total <= kMaxWarps * 4u * kLimbPasses) {
+            p.type = type;
+            p.wide = true;
+            p.slice = true;
+            p.warps = kMaxWarps;
+            p.team = 1;
+            p.tokens = 1;
+            p.seg_pairs = static_cast<uint32_t>(up);
+            p.tile_rows = kTileRows;
+            p.tiles = static_cast<uint32_t>(tiles);
+            p.slots = static_cast<uint32_t>(slots);
+            p.unit_bytes = static_cast<uint32_t>(unit);
+            p.box_bytes = static_cast<uint32_t>(box);
+            p.grid = static_cast<uint32_t>(grid);
+            p.smem_bytes = static_cast<uint32_t>(smem);
+            p.groups = 1;
+            p.group_pairs = static_cast<uint32_t>(pairs_total);
+            p.tile_group = tiles_per_cta > 2 ? 5u : 2u;
+            // Copies issued before x is requested: x's loads queue behind this SM's
+            // earlier weight copies, so only about as much as lands while the CTA
+            // waits for the previous kernel (measured: ~150 KB) goes out first.
+            const uint64_t chunk_bytes = tiles_per_cta * unit;
+            uint64_t early = kEarlyBytes / chunk_bytes;
+            if (early < 1) early = 1;
+            p.early_chunks = static_cast<uint32_t>(early < nchunk ? early : nchunk);
+            p.ok = true;
+            return p;
+        }
+    }
     // consumer warps: 16 for one token; 8 for several (each unit's MMA work grows with
     // the tokens, and 4 warps already keep the SM's int8 MMA pipe busy)
     const uint64_t max_warps = tokens == 1 ? kMaxWarps : 8u;
@@ -769,6 +1189,11 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
     a.ldx = ldx;
     a.ldy = ldy;
     a.status = status;
+    a.early_chunks = plan.early_chunks;
+    if (plan.slice) {
+        if (plan.type == kQ8_0) return launch_slice_p<kQ8_0>(plan, map, a, stream, pdl);
+        return launch_slice_p<kQ4_0>(plan, map, a, stream, pdl);
+    }
     if (plan.type == kQ8_0) return launch_imma_p<kQ8_0>(plan, map, a, stream, pdl);
     return launch_imma_p<kQ4_0>(plan, map, a, stream, pdl);
 }

@@ -60,6 +60,9 @@ cudaError_t launch_stream(uint32_t type, const StreamPlan& plan, const void* w, 
 struct ImmaPlan {
     bool ok = false;
     bool wide = false;         // ring sized for the whole SM (else two CTAs fit on an SM)
+    bool slice = false;        // resident slice: every unit of a CTA in its own slot (gemv_imma_slice_kernel)
+    uint32_t tile_group = 0;   // slice: tiles sharing one read of the x side
+    uint32_t early_chunks = 0; // slice: column chunks copied before x is requested
     uint32_t type = 0;
     uint32_t warps = 0;        // consumer warps; one more warp streams units
     uint32_t team = 0;         // warps sharing one tile (its segments split among them)
@@ -78,6 +81,7 @@ struct ImmaPlan {
 
 struct ImmaTuning {
     int wide = -1;             // 1 = ring sized for the whole SM
+    int slice = -1;            // 0 = never the resident-slice kernel
     uint32_t ctas_per_sm = 0;  // grid = SMs x this (at most the tile count)
     uint32_t slots = 0;
     uint32_t seg_pairs = 0;    // 8 or 16
