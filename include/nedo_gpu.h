@@ -268,6 +268,71 @@ NEDO_GPU_API int nedo_gpu_status(void* stream);
  * n = capacity of out (>= 8). */
 NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
 
+/* ---- Device-resident decode forward pass -------------------------------
+ *
+ * Replaces the `forward` step of NedoModel::generate_ids (src/model.cpp:212-260):
+ * embedding row, then per layer RMSNorm, q/k/v projections, RoPE, the KV-cache
+ * write, attention over the sliding window, the output projection and residual,
+ * RMSNorm, gate/up projections, SiLU gate (with the MorphFFN masking of the
+ * trailing layers, :196-209), the down projection and residual; then the final
+ * RMSNorm and the LM-head matvec.  Weights and the fp32 KV cache stay on the
+ * device; one call runs the whole pass as one CUDA graph (captured on the first
+ * call, the token and position read from device memory) and returns the greedy
+ * pick and, on request, the logits.
+ *
+ * The configuration mirrors ModelConfig (include/nedo/model.hpp:12-16). */
+typedef struct {
+    uint32_t vocab, dim, layers, heads, kv_heads, head_dim, ffn, context, sliding;
+    uint32_t morph_layers, morph_shared, morph_root, morph_suffix;
+    float rms_eps, rope_theta;
+} nedo_gpu_decoder_config;
+
+/* One GGUF tensor: TensorInfo's type and shape (contiguous dimension first)
+ * and a host view of its bytes (e.g. GgufFile::bytes, src/gguf.cpp:139). */
+typedef struct {
+    uint32_t type;
+    uint32_t ndims;
+    uint64_t shape[2];
+    const void* data;
+    uint64_t nbytes;
+} nedo_gpu_tensor_view;
+
+/* Tensor order of nedo_gpu_decoder_create:
+ *   [0] token_embd (F16 / Q8_0 / Q4_0), [1] output_norm (F32 / F16),
+ *   [2] output (F16 / Q8_0 / Q4_0; data NULL: the head is token_embd),
+ *   [3] blk.0.ffn_gate_tid2eid, the MorphFFN routing table (F32 [2, vocab];
+ *       data NULL: none),
+ *   then 9 per layer: attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm,
+ *   ffn_gate, ffn_up, ffn_down (norms F32 / F16, projections F16 / Q8_0 / Q4_0;
+ *   q, k, v of one type, gate and up of one type).
+ * Shape and type checks follow the reference: "invalid GQA dimensions"
+ * (heads % kv_heads, dim == heads * head_dim), "context_length is zero",
+ * "MorphFFN widths do not sum to feed_forward_length", and every tensor's
+ * shape against the configuration.  The weights are copied to the device; the
+ * host views may be released afterwards. */
+typedef struct nedo_gpu_decoder nedo_gpu_decoder;
+NEDO_GPU_API int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_tensor_view* tensors,
+                                         uint64_t ntensors, nedo_gpu_decoder** out);
+
+/* One forward pass for `token` at position `pos` (positions from 0, one per
+ * call, as generate_ids: the KV-cache slot is pos % window with window =
+ * min(sliding ? sliding : context, context)).  *argmax_out (if non-null) gets
+ * the greedy pick (std::max_element semantics: first index of the maximum);
+ * logits_host (if non-null) gets the vocab logits.  token >= vocab
+ * ("prompt token id out of range") and pos >= context are NEDO_GPU_ERR_ARG. */
+NEDO_GPU_API int nedo_gpu_decoder_forward(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, float* logits_host,
+                                          uint32_t* argmax_out);
+
+/* The logits of the last forward pass in device memory (valid until the next
+ * call), for the sampler entry points (nedo_gpu_topk_dev). */
+NEDO_GPU_API int nedo_gpu_decoder_logits_dev(nedo_gpu_decoder* d, const float** logits_dev);
+
+/* Zero the KV cache (a new sequence starts at pos 0 either way). */
+NEDO_GPU_API int nedo_gpu_decoder_reset(nedo_gpu_decoder* d);
+
+/* Free the decoder's device memory and graphs (NULL is a no-op). */
+NEDO_GPU_API void nedo_gpu_decoder_destroy(nedo_gpu_decoder* d);
+
 #ifdef __cplusplus
 }
 #endif

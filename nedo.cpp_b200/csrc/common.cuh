@@ -17,6 +17,7 @@ enum : uint32_t { kF16 = 1, kQ4_0 = 2, kQ8_0 = 8 };
 enum : uint32_t {
     kErrWaitTimeout = 1u,   // an mbarrier wait exceeded its time bound
     kErrBadLaunch = 2u,     // a kernel saw launch parameters it cannot honour
+    kErrArgument = 4u,      // a kernel read an out-of-range value from device memory (a token id)
 };
 
 struct DeviceStatus {

@@ -186,6 +186,30 @@ cudaError_t launch_splitk_reduce(const float* ws, float* y, uint32_t splits, uin
 
 uint64_t row_bytes_of(uint32_t type, uint64_t cols);
 
+// ---- decode forward (decode.cu) ----
+// The per-step inputs of a captured decode graph, in device memory.
+struct DecodeIo {
+    uint64_t pos;
+    uint32_t token;
+    uint32_t pad;
+};
+// x = embedding row io->token (F16 / Q8_0 / Q4_0 rows of `cols`; an id >= rows sets kErrArgument).
+cudaError_t launch_embed(uint32_t type, const void* w, uint64_t cols, uint64_t rows, const DecodeIo* io, float* x,
+                         DeviceStatus* st, cudaStream_t stream, bool pdl);
+// x += delta (delta may be null), y = RMSNorm(x) * w (w F32, wtype 0, or F16, wtype 1).
+cudaError_t launch_add_rmsnorm(float* x, const float* delta, const void* w, uint32_t wtype, float* y, uint32_t n,
+                               float eps, cudaStream_t stream, bool pdl);
+// RoPE on q and k of qkv = [q (nq x hd) | k (nkv x hd) | v (nkv x hd)], k and v into slot io->pos % window.
+cudaError_t launch_rope_kv(float* qkv, uint32_t nq, uint32_t nkv, uint32_t hd, float theta, const DecodeIo* io,
+                           float* kcache, float* vcache, uint32_t window, cudaStream_t stream, bool pdl);
+size_t attention_smem_bytes(uint32_t window, uint32_t hd);
+cudaError_t launch_attention(const float* qkv, const float* kcache, const float* vcache, float* att,
+                             const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd, uint32_t window,
+                             float inv_sqrt_hd, cudaStream_t stream, bool pdl);
+// gu = [gate | up] (f each): gate = silu(gate) * up, MorphFFN masks when route is non-null.
+cudaError_t launch_silu_mul(float* gu, uint32_t f, const float* route, const DecodeIo* io, uint32_t shared_w,
+                            uint32_t root_w, uint32_t suffix_w, cudaStream_t stream, bool pdl);
+
 // cuTensorMapEncodeTiled reached through the runtime's driver entry point
 // (null when the driver does not provide it).
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -7,6 +7,7 @@
 // the streaming kernel, the batched tensor-core kernel and the generic kernel.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <atomic>
@@ -968,6 +969,422 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     }
     out[0] = batch > 1 ? 3 : 2;
     return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Device-resident decode forward pass (src/model.cpp:212-260).
+//
+// Layout in HBM: every weight uploaded once; q, k and v of a layer stored as
+// one [q | k | v] matrix and gate and up as one [gate | up] matrix, so each pair
+// or triple that shares its input is one matvec launch (rows concatenated, row
+// bytes unchanged); the fp32 KV cache [layer][window][kv_heads * head_dim] for
+// keys and for values; fp32 activations x, xn, qkv, att, tmp, gu and the logits.
+// A pass is 2 + 9 * layers launches on one stream (programmatic dependent
+// launch between them), captured once as a CUDA graph that also uploads the
+// token and position and downloads the greedy pick and the status word.
+namespace {
+
+struct DecLayer {
+    uint32_t an_type = 0, fn_type = 0, qkv_type = 0, o_type = 0, gu_type = 0, down_type = 0;
+    const void *an = nullptr, *fn = nullptr, *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+};
+
+struct DecPin {
+    DecodeIo io;
+    int64_t index;
+    float value;
+    uint32_t pad;
+    DeviceStatus status;
+};
+
+}  // namespace
+
+struct nedo_gpu_decoder {
+    DeviceState* s = nullptr;
+    nedo_gpu_decoder_config cfg{};
+    uint32_t window = 0, qd = 0, kvd = 0;
+    uint64_t emb_rows = 0, head_rows = 0;
+    uint32_t emb_type = 0, onorm_type = 0, head_type = 0;
+    const void *emb = nullptr, *onorm = nullptr, *head = nullptr;
+    const float* route = nullptr;
+    std::vector<DecLayer> layers;
+    std::vector<void*> owned;
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *tmp = nullptr, *gu = nullptr;
+    float *logits = nullptr, *kcache = nullptr, *vcache = nullptr;
+    DecodeIo* io = nullptr;
+    int64_t* amax = nullptr;  // index, then the value (float) in the next 8 bytes
+    ArgmaxScratch scratch{};
+    DecPin* pin = nullptr;
+    float* logits_pin = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t graph[2] = {nullptr, nullptr};  // without / with the logits download
+    bool eager_done[2] = {false, false};
+};
+
+namespace {
+
+int dec_alloc(nedo_gpu_decoder* d, void** p, uint64_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(decoder)");
+    d->owned.push_back(*p);
+    return 0;
+}
+
+// Upload one or more tensors back to back into one device buffer.
+int dec_upload(nedo_gpu_decoder* d, const nedo_gpu_tensor_view* const* parts, int n, const void** out) {
+    uint64_t total = 0;
+    for (int i = 0; i < n; ++i) total += parts[i]->nbytes;
+    void* dev = nullptr;
+    if (int rc = dec_alloc(d, &dev, total)) return rc;
+    uint64_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        if (int rc = upload_weight(d->s, static_cast<uint8_t*>(dev) + off, parts[i]->data, parts[i]->nbytes)) return rc;
+        off += parts[i]->nbytes;
+    }
+    *out = dev;
+    return 0;
+}
+
+std::string tensor_label(uint64_t i) {
+    static const char* kTop[4] = {"token_embd.weight", "output_norm.weight", "output.weight",
+                                  "blk.0.ffn_gate_tid2eid.weight"};
+    static const char* kLayer[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                    "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+    if (i < 4) return kTop[i];
+    return "blk." + std::to_string((i - 4) / 9) + "." + kLayer[(i - 4) % 9] + ".weight";
+}
+
+// A rank-2 projection [cols, rows] of a matvec type, its bytes the rows' bytes.
+int check_matrix(const nedo_gpu_tensor_view& t, uint64_t i, uint64_t cols, uint64_t rows) {
+    const std::string name = tensor_label(i);
+    if (t.data == nullptr) return fail(NEDO_GPU_ERR_ARG, "missing tensor: " + name);
+    if (t.ndims != 2) return fail(NEDO_GPU_ERR_ARG, "matvec requires rank-2 tensor: " + name);
+    if (!is_matvec_type(t.type)) return fail(NEDO_GPU_ERR_TYPE, "matvec tensor type not supported: " + name);
+    uint64_t rb = 0;
+    if (int rc = tensor_row_bytes(t.type, t.shape[0], &rb)) return rc;
+    if (t.shape[0] != cols || t.shape[1] != rows || t.nbytes != rb * rows)
+        return fail(NEDO_GPU_ERR_ARG, "tensor shape does not match the configuration: " + name);
+    return 0;
+}
+
+int check_norm(const nedo_gpu_tensor_view& t, uint64_t i, uint64_t n) {
+    const std::string name = tensor_label(i);
+    if (t.data == nullptr) return fail(NEDO_GPU_ERR_ARG, "missing tensor: " + name);
+    if (t.ndims != 1 || t.shape[0] != n) return fail(NEDO_GPU_ERR_ARG, "bad RMSNorm tensor: " + name);
+    if (t.type != 0 && t.type != kF16) return fail(NEDO_GPU_ERR_TYPE, "unsupported RMSNorm tensor type: " + name);
+    if (t.nbytes != n * (t.type == 0 ? 4u : 2u)) return fail(NEDO_GPU_ERR_ARG, "bad RMSNorm tensor: " + name);
+    return 0;
+}
+
+// The pass, enqueued on d->stream (captured or eager).
+int dec_enqueue(nedo_gpu_decoder* d) {
+    DeviceState* s = d->s;
+    const nedo_gpu_decoder_config& c = d->cfg;
+    cudaStream_t st = d->stream;
+    const bool pdl = true;
+    const uint32_t hd = c.head_dim;
+    const float inv_sqrt_hd = 1.0f / std::sqrt(static_cast<float>(hd));
+    cudaError_t e = launch_embed(d->emb_type, d->emb, c.dim, d->emb_rows, d->io, d->x, s->status, st, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, "embedding launch");
+    const size_t cache_layer = static_cast<size_t>(d->window) * d->kvd;
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        const DecLayer& L = d->layers[li];
+        e = launch_add_rmsnorm(d->x, li ? d->tmp : nullptr, L.an, L.an_type == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps,
+                               st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+        if (int rc = dispatch_matvec(s, L.qkv_type, d->qd + 2u * d->kvd, c.dim, L.qkv, d->xn, d->qkv, 1, nullptr, st, 1))
+            return rc;
+        float* kc = d->kcache + li * cache_layer;
+        float* vc = d->vcache + li * cache_layer;
+        e = launch_rope_kv(d->qkv, c.heads, c.kv_heads, hd, c.rope_theta, d->io, kc, vc, d->window, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+        e = launch_attention(d->qkv, kc, vc, d->att, d->io, c.heads, c.kv_heads, hd, d->window, inv_sqrt_hd, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+        if (int rc = dispatch_matvec(s, L.o_type, c.dim, d->qd, L.o, d->att, d->tmp, 1, nullptr, st, 1)) return rc;
+        e = launch_add_rmsnorm(d->x, d->tmp, L.fn, L.fn_type == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+        if (int rc = dispatch_matvec(s, L.gu_type, 2u * c.ffn, c.dim, L.gu, d->xn, d->gu, 1, nullptr, st, 1))
+            return rc;
+        // MorphFFN occupies the trailing morph_layers blocks (src/model.cpp:200)
+        const bool morph = d->route != nullptr && li + c.morph_layers >= c.layers;
+        e = launch_silu_mul(d->gu, c.ffn, morph ? d->route : nullptr, d->io, c.morph_shared, c.morph_root,
+                            c.morph_suffix, st, pdl);
+        if (e != cudaSuccess) return cuda_fail(e, "silu launch");
+        if (int rc = dispatch_matvec(s, L.down_type, c.dim, c.ffn, L.down, d->gu, d->tmp, 1, nullptr, st, 1))
+            return rc;
+    }
+    e = launch_add_rmsnorm(d->x, c.layers ? d->tmp : nullptr, d->onorm, d->onorm_type == 0 ? 0u : 1u, d->xn, c.dim,
+                           c.rms_eps, st, pdl);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+    ArgmaxScratch a = d->scratch;
+    a.out_index = d->amax;
+    a.out_value = reinterpret_cast<float*>(d->amax + 1);
+    return dispatch_matvec(s, d->head_type, d->head_rows, c.dim, d->head, d->xn, d->logits, 1, &a, st, 1);
+}
+
+// io upload, the pass, the result and status downloads (and the logits).
+int dec_step_ops(nedo_gpu_decoder* d, bool with_logits) {
+    NEDO_CUDA_TRY(cudaMemcpyAsync(d->io, &d->pin->io, sizeof(DecodeIo), cudaMemcpyHostToDevice, d->stream));
+    if (int rc = dec_enqueue(d)) return rc;
+    NEDO_CUDA_TRY(cudaMemcpyAsync(&d->pin->index, d->amax, sizeof(int64_t) + sizeof(float), cudaMemcpyDeviceToHost,
+                                  d->stream));
+    NEDO_CUDA_TRY(cudaMemcpyAsync(&d->pin->status, d->s->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost,
+                                  d->stream));
+    if (with_logits)
+        NEDO_CUDA_TRY(cudaMemcpyAsync(d->logits_pin, d->logits, d->head_rows * sizeof(float), cudaMemcpyDeviceToHost,
+                                      d->stream));
+    return 0;
+}
+
+void dec_free(nedo_gpu_decoder* d) {
+    for (auto& g : d->graph)
+        if (g) cudaGraphExecDestroy(g);
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    for (void* p : d->owned) cudaFree(p);
+    if (d->pin) cudaFreeHost(d->pin);
+    if (d->logits_pin) cudaFreeHost(d->logits_pin);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    delete d;
+}
+
+// Runs `fn` with the decoder's device current, restoring the caller's.
+template <typename F>
+int on_device(int dev, F fn) {
+    int prev = 0;
+    NEDO_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != dev) NEDO_CUDA_TRY(cudaSetDevice(dev));
+    const int rc = fn();
+    if (prev != dev) cudaSetDevice(prev);
+    return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_tensor_view* t, uint64_t n,
+                            nedo_gpu_decoder** out) {
+    if (!cfg || !t || !out) return fail(NEDO_GPU_ERR_ARG, "decoder_create: null pointer");
+    *out = nullptr;
+    const nedo_gpu_decoder_config c = *cfg;
+    // src/model.cpp:158-160
+    if (!c.heads || !c.kv_heads || c.heads % c.kv_heads || c.dim != c.heads * c.head_dim)
+        return fail(NEDO_GPU_ERR_ARG, "invalid GQA dimensions");
+    if (!c.context) return fail(NEDO_GPU_ERR_ARG, "context_length is zero");
+    if (c.head_dim % 2u || c.head_dim > 512u) return fail(NEDO_GPU_ERR_ARG, "head_dim must be even and at most 512");
+    if (c.dim == 0 || c.ffn == 0 || c.vocab == 0) return fail(NEDO_GPU_ERR_ARG, "empty model dimensions");
+    if (n != 4u + 9ull * c.layers) return fail(NEDO_GPU_ERR_ARG, "decoder_create: expected 4 + 9 * layers tensors");
+    const uint32_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
+    // embedding and head
+    if (t[0].data == nullptr || t[0].ndims != 2 || t[0].shape[0] != c.dim || t[0].shape[1] < c.vocab)
+        return fail(NEDO_GPU_ERR_ARG, "bad embedding tensor: token_embd.weight");
+    if (!is_matvec_type(t[0].type)) return fail(NEDO_GPU_ERR_TYPE, "embedding type unsupported");
+    if (int rc = check_matrix(t[0], 0, c.dim, t[0].shape[1])) return rc;
+    if (int rc = check_norm(t[1], 1, c.dim)) return rc;
+    const nedo_gpu_tensor_view& head = t[2].data ? t[2] : t[0];
+    if (int rc = check_matrix(head, t[2].data ? 2 : 0, c.dim, head.shape[1])) return rc;
+    if (head.shape[1] < c.vocab) return fail(NEDO_GPU_ERR_ARG, "LM head has fewer rows than vocab_size");
+    if (t[3].data) {
+        if (t[3].type != 0 || t[3].ndims != 2 || t[3].shape[0] != 2 || t[3].shape[1] != c.vocab ||
+            t[3].nbytes != 8ull * c.vocab)
+            return fail(NEDO_GPU_ERR_ARG, "MorphFFN token-id routing table shape/type [2,vocab] F32");
+        if (c.morph_shared + c.morph_root + c.morph_suffix != c.ffn)
+            return fail(NEDO_GPU_ERR_ARG, "MorphFFN widths do not sum to feed_forward_length");
+        if (c.morph_layers > c.layers) return fail(NEDO_GPU_ERR_ARG, "MorphFFN layer count exceeds block count");
+    }
+    for (uint32_t li = 0; li < c.layers; ++li) {
+        const uint64_t b = 4ull + 9ull * li;
+        if (int rc = check_norm(t[b + 0], b + 0, c.dim)) return rc;
+        if (int rc = check_matrix(t[b + 1], b + 1, c.dim, qd)) return rc;
+        if (int rc = check_matrix(t[b + 2], b + 2, c.dim, kvd)) return rc;
+        if (int rc = check_matrix(t[b + 3], b + 3, c.dim, kvd)) return rc;
+        if (int rc = check_matrix(t[b + 4], b + 4, qd, c.dim)) return rc;
+        if (int rc = check_norm(t[b + 5], b + 5, c.dim)) return rc;
+        if (int rc = check_matrix(t[b + 6], b + 6, c.dim, c.ffn)) return rc;
+        if (int rc = check_matrix(t[b + 7], b + 7, c.dim, c.ffn)) return rc;
+        if (int rc = check_matrix(t[b + 8], b + 8, c.ffn, c.dim)) return rc;
+        if (t[b + 1].type != t[b + 2].type || t[b + 1].type != t[b + 3].type)
+            return fail(NEDO_GPU_ERR_TYPE, "q, k and v projections of a layer must share one type");
+        if (t[b + 6].type != t[b + 7].type)
+            return fail(NEDO_GPU_ERR_TYPE, "gate and up projections of a layer must share one type");
+    }
+    const uint32_t sl = c.sliding ? c.sliding : c.context;
+    const uint32_t window = std::max<uint32_t>(1u, std::min<uint32_t>(sl, c.context));
+    if (attention_smem_bytes(window, c.head_dim) > 200u * 1024u)
+        return fail(NEDO_GPU_ERR_ARG, "attention window too long for one CTA's shared memory");
+
+    DeviceState* s = nullptr;
+    if (int rc = get_state(&s)) return rc;
+    auto* d = new nedo_gpu_decoder();
+    d->s = s;
+    d->cfg = c;
+    d->window = window;
+    d->qd = qd;
+    d->kvd = kvd;
+    auto build = [&]() -> int {
+        NEDO_CUDA_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+        const nedo_gpu_tensor_view* p1[1];
+        p1[0] = &t[0];
+        if (int rc = dec_upload(d, p1, 1, &d->emb)) return rc;
+        d->emb_type = t[0].type;
+        d->emb_rows = t[0].shape[1];
+        p1[0] = &t[1];
+        if (int rc = dec_upload(d, p1, 1, &d->onorm)) return rc;
+        d->onorm_type = t[1].type;
+        if (t[2].data) {
+            p1[0] = &t[2];
+            if (int rc = dec_upload(d, p1, 1, &d->head)) return rc;
+        } else {
+            d->head = d->emb;  // tied (src/model.cpp:94)
+        }
+        d->head_type = head.type;
+        d->head_rows = head.shape[1];
+        if (t[3].data) {
+            const void* r = nullptr;
+            p1[0] = &t[3];
+            if (int rc = dec_upload(d, p1, 1, &r)) return rc;
+            d->route = static_cast<const float*>(r);
+        }
+        d->layers.resize(c.layers);
+        for (uint32_t li = 0; li < c.layers; ++li) {
+            const uint64_t b = 4ull + 9ull * li;
+            DecLayer& L = d->layers[li];
+            p1[0] = &t[b + 0];
+            if (int rc = dec_upload(d, p1, 1, &L.an)) return rc;
+            L.an_type = t[b + 0].type;
+            const nedo_gpu_tensor_view* qkv[3] = {&t[b + 1], &t[b + 2], &t[b + 3]};
+            if (int rc = dec_upload(d, qkv, 3, &L.qkv)) return rc;
+            L.qkv_type = t[b + 1].type;
+            p1[0] = &t[b + 4];
+            if (int rc = dec_upload(d, p1, 1, &L.o)) return rc;
+            L.o_type = t[b + 4].type;
+            p1[0] = &t[b + 5];
+            if (int rc = dec_upload(d, p1, 1, &L.fn)) return rc;
+            L.fn_type = t[b + 5].type;
+            const nedo_gpu_tensor_view* gu[2] = {&t[b + 6], &t[b + 7]};
+            if (int rc = dec_upload(d, gu, 2, &L.gu)) return rc;
+            L.gu_type = t[b + 6].type;
+            p1[0] = &t[b + 8];
+            if (int rc = dec_upload(d, p1, 1, &L.down)) return rc;
+            L.down_type = t[b + 8].type;
+        }
+        void* p = nullptr;
+        auto vec = [&](float** f, uint64_t count) -> int {
+            if (int rc = dec_alloc(d, &p, count * sizeof(float))) return rc;
+            *f = static_cast<float*>(p);
+            return 0;
+        };
+        if (int rc = vec(&d->x, c.dim)) return rc;
+        if (int rc = vec(&d->xn, c.dim)) return rc;
+        if (int rc = vec(&d->qkv, qd + 2ull * kvd)) return rc;
+        if (int rc = vec(&d->att, qd)) return rc;
+        if (int rc = vec(&d->tmp, c.dim)) return rc;
+        if (int rc = vec(&d->gu, 2ull * c.ffn)) return rc;
+        if (int rc = vec(&d->logits, d->head_rows)) return rc;
+        const uint64_t cache = static_cast<uint64_t>(c.layers) * window * kvd;
+        if (int rc = vec(&d->kcache, cache ? cache : 1)) return rc;
+        if (int rc = vec(&d->vcache, cache ? cache : 1)) return rc;
+        NEDO_CUDA_TRY(cudaMemsetAsync(d->kcache, 0, (cache ? cache : 1) * sizeof(float), d->stream));
+        NEDO_CUDA_TRY(cudaMemsetAsync(d->vcache, 0, (cache ? cache : 1) * sizeof(float), d->stream));
+        if (int rc = dec_alloc(d, &p, sizeof(DecodeIo))) return rc;
+        d->io = static_cast<DecodeIo*>(p);
+        if (int rc = dec_alloc(d, &p, 16)) return rc;
+        d->amax = static_cast<int64_t*>(p);
+        const size_t ncand = static_cast<size_t>(s->num_sms) + 1;
+        if (int rc = dec_alloc(d, &p, ncand * sizeof(float))) return rc;
+        d->scratch.cand_val = static_cast<float*>(p);
+        if (int rc = dec_alloc(d, &p, ncand * sizeof(uint32_t))) return rc;
+        d->scratch.cand_idx = static_cast<uint32_t*>(p);
+        if (int rc = dec_alloc(d, &p, sizeof(uint32_t))) return rc;
+        d->scratch.counter = static_cast<uint32_t*>(p);
+        NEDO_CUDA_TRY(cudaMemsetAsync(d->scratch.counter, 0, sizeof(uint32_t), d->stream));
+        NEDO_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&d->pin), sizeof(DecPin), cudaHostAllocDefault));
+        NEDO_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&d->logits_pin), d->head_rows * sizeof(float),
+                                    cudaHostAllocDefault));
+        NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        return 0;
+    };
+    if (int rc = build()) {
+        dec_free(d);
+        return rc;
+    }
+    *out = d;
+    return 0;
+}
+
+int nedo_gpu_decoder_forward(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, float* logits_host,
+                             uint32_t* argmax_out) {
+    if (!d) return fail(NEDO_GPU_ERR_ARG, "decoder_forward: null decoder");
+    if (token >= d->cfg.vocab || token >= d->emb_rows) return fail(NEDO_GPU_ERR_ARG, "prompt token id out of range");
+    if (pos >= d->cfg.context) return fail(NEDO_GPU_ERR_ARG, "position beyond context_length");
+    return on_device(d->s->device, [&]() -> int {
+        d->pin->io.pos = pos;
+        d->pin->io.token = token;
+        const int k = logits_host ? 1 : 0;
+        if (d->graph[k] == nullptr && d->eager_done[k]) {
+            // second call of this kind: capture the pass once (it re-reads io from device memory)
+            cudaGraph_t g = nullptr;
+            NEDO_CUDA_TRY(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
+            const int rc = dec_step_ops(d, k == 1);
+            cudaError_t e = cudaStreamEndCapture(d->stream, &g);
+            if (rc) {
+                if (g) cudaGraphDestroy(g);
+                return rc;
+            }
+            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture(decoder)");
+            e = cudaGraphInstantiate(&d->graph[k], g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate(decoder)");
+        }
+        if (d->graph[k]) {
+            NEDO_CUDA_TRY(cudaGraphLaunch(d->graph[k], d->stream));
+        } else {
+            // first call of this kind runs eagerly (kernel attributes and plans settle)
+            if (int rc = dec_step_ops(d, k == 1)) return rc;
+            d->eager_done[k] = true;
+        }
+        NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        if (d->pin->status.flags != 0) {
+            const DeviceStatus st = d->pin->status;
+            clear_status_flags(d->s, d->stream);
+            char buf[160];
+            std::snprintf(buf, sizeof(buf), "device kernel failed in the decode pass (flags=0x%x, site=%u)", st.flags,
+                          st.where);
+            return fail(NEDO_GPU_ERR_DEVICE, buf);
+        }
+        if (argmax_out) *argmax_out = static_cast<uint32_t>(d->pin->index);
+        if (logits_host) std::memcpy(logits_host, d->logits_pin, d->head_rows * sizeof(float));
+        return 0;
+    });
+}
+
+int nedo_gpu_decoder_logits_dev(nedo_gpu_decoder* d, const float** logits_dev) {
+    if (!d || !logits_dev) return fail(NEDO_GPU_ERR_ARG, "decoder_logits_dev: null pointer");
+    *logits_dev = d->logits;
+    return 0;
+}
+
+int nedo_gpu_decoder_reset(nedo_gpu_decoder* d) {
+    if (!d) return fail(NEDO_GPU_ERR_ARG, "decoder_reset: null decoder");
+    return on_device(d->s->device, [&]() -> int {
+        const size_t bytes = static_cast<size_t>(d->cfg.layers) * d->window * d->kvd * sizeof(float);
+        if (bytes) {
+            NEDO_CUDA_TRY(cudaMemsetAsync(d->kcache, 0, bytes, d->stream));
+            NEDO_CUDA_TRY(cudaMemsetAsync(d->vcache, 0, bytes, d->stream));
+        }
+        NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        return 0;
+    });
+}
+
+void nedo_gpu_decoder_destroy(nedo_gpu_decoder* d) {
+    if (!d) return;
+    on_device(d->s->device, [&]() -> int {
+        dec_free(d);
+        return 0;
+    });
 }
 
 }  // extern "C"

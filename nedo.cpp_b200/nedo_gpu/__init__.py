@@ -56,6 +56,11 @@ EXPORTS = (
     "nedo_gpu_dequant_rows_dev",
     "nedo_gpu_status",
     "nedo_gpu_plan_info",
+    "nedo_gpu_decoder_create",
+    "nedo_gpu_decoder_forward",
+    "nedo_gpu_decoder_logits_dev",
+    "nedo_gpu_decoder_reset",
+    "nedo_gpu_decoder_destroy",
 )
 
 
@@ -70,6 +75,20 @@ class NedoGpuError(RuntimeError):
 _u32, _u64, _i32, _vp = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p
 _f32p = ctypes.POINTER(ctypes.c_float)
 _u64p = ctypes.POINTER(ctypes.c_uint64)
+
+class DecoderConfig(ctypes.Structure):
+    """nedo_gpu_decoder_config (ModelConfig, include/nedo/model.hpp:12-16)."""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("vocab", "dim", "layers", "heads", "kv_heads", "head_dim", "ffn",
+                                                "context", "sliding", "morph_layers", "morph_shared", "morph_root",
+                                                "morph_suffix")] + [("rms_eps", ctypes.c_float),
+                                                                    ("rope_theta", ctypes.c_float)]
+
+
+class TensorView(ctypes.Structure):
+    """nedo_gpu_tensor_view: a GGUF tensor's type, shape and host bytes."""
+    _fields_ = [("type", ctypes.c_uint32), ("ndims", ctypes.c_uint32), ("shape", ctypes.c_uint64 * 2),
+                ("data", ctypes.c_void_p), ("nbytes", ctypes.c_uint64)]
+
 
 _SIGNATURES = {
     "nedo_gpu_version": ([], _i32),
@@ -96,6 +115,12 @@ _SIGNATURES = {
     "nedo_gpu_dequant_rows_dev": ([_u32, _u64, _u64, _vp, _u64, _u64, _vp, _vp], _i32),
     "nedo_gpu_status": ([_vp], _i32),
     "nedo_gpu_plan_info": ([_u32, _u64, _u64, _u32, ctypes.POINTER(_u32), _i32], _i32),
+    "nedo_gpu_decoder_create": ([ctypes.POINTER(DecoderConfig), ctypes.POINTER(TensorView), _u64, ctypes.POINTER(_vp)],
+                                _i32),
+    "nedo_gpu_decoder_forward": ([_vp, _u32, _u64, _vp, ctypes.POINTER(_u32)], _i32),
+    "nedo_gpu_decoder_logits_dev": ([_vp, ctypes.POINTER(_vp)], _i32),
+    "nedo_gpu_decoder_reset": ([_vp], _i32),
+    "nedo_gpu_decoder_destroy": ([_vp], None),
 }
 
 

@@ -1,0 +1,132 @@
+"""The device-resident decode forward pass (nedo_gpu_decoder_*) against the
+reference's own decode loop (src/model.cpp:151-281).
+
+For each synthetic model of tests/golden/decode_golden.npz (Q8_0 / Q4_0 / F16
+weights, GQA and MHA, tied head, a sliding window shorter than the sequence,
+MorphFFN masking) the decoder runs the reference's token sequence (prompt,
+then the reference's greedy ids, teacher-forced) and every pass's logits are
+compared with the reference's: |delta| <= LOGIT_TOL * max|logit| per pass.
+The tolerance covers the matvec kernels' exact-limb int8 arithmetic (each
+output within 1e-4 * sum|w*x| of the reference, in practice 1e-6), float
+transcendentals and a different summation order in RMSNorm, softmax and the
+attention sums, compounded over the layers.  The decoder's greedy pick must
+be the first index of its own logits' maximum, and the reference's pick
+wherever the reference's top-2 gap exceeds the tolerance.  The free-running
+greedy decode is then checked against the reference's ids, and a rerun after
+reset must give bit-identical logits (the captured graph replays the eager
+first pass)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+sys.path[:0] = [os.path.join(ROOT, "tests", "golden")]
+import make_decode_golden as M  # noqa: E402
+import nedo_gpu  # noqa: E402
+from nedo_gpu import gguf as G  # noqa: E402
+from nedo_gpu.decoder import Decoder, config_from_gguf  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(os.path.join(ROOT, "tests", "golden", "decode_golden.npz"))
+LOGIT_TOL = 2e-4
+
+
+@pytest.fixture(scope="module", params=list(M.MODELS))
+def model(request, tmp_path_factory, cuda):
+    name = request.param
+    kw, prompt, max_new = M.MODELS[name]
+    p = str(tmp_path_factory.mktemp("dec") / (name + ".gguf"))
+    G.synthetic_model(p, **kw)
+    g = G.GgufFile(p)
+    dec = Decoder.from_gguf(g)
+    yield name, g, dec, prompt, max_new
+    dec.close()
+
+
+def test_teacher_forced_logits_match_reference(model):
+    name, g, dec, prompt, max_new = model
+    ref = GOLDEN[name + "/logits"]
+    ids = list(GOLDEN[name + "/ids"])
+    seq = list(prompt) + ids
+    dec.reset()
+    worst = 0.0
+    for pos in range(ref.shape[0]):
+        pick, lg = dec.forward(seq[pos], pos)
+        scale = float(np.abs(ref[pos]).max())
+        err = float(np.abs(lg - ref[pos]).max()) / scale
+        worst = max(worst, err)
+        assert err <= LOGIT_TOL, (name, pos, err)
+        assert pick == int(np.argmax(lg))
+        s = np.sort(ref[pos])
+        if s[-1] - s[-2] > 4 * LOGIT_TOL * scale:
+            assert pick == int(np.argmax(ref[pos])), (name, pos)
+    print(f"{name}: worst logit error {worst:.2e} of max |logit|")
+
+
+def test_greedy_matches_reference_ids(model):
+    name, g, dec, prompt, max_new = model
+    dec.reset()
+    _, ids = dec.greedy(prompt, max_new, logits=False)
+    assert ids == [int(i) for i in GOLDEN[name + "/ids"]]
+
+
+def test_rerun_is_bit_identical(model):
+    name, g, dec, prompt, max_new = model
+    seq = list(prompt) + [int(i) for i in GOLDEN[name + "/ids"]]
+    runs = []
+    for _ in range(2):
+        dec.reset()
+        runs.append(np.stack([dec.forward(t, p)[1] for p, t in enumerate(seq[:8])]))
+    assert np.array_equal(runs[0].view(np.uint32), runs[1].view(np.uint32))
+
+
+def test_decoder_argument_errors(model):
+    name, g, dec, prompt, max_new = model
+    with pytest.raises(nedo_gpu.NedoGpuError) as e:
+        dec.forward(dec.cfg.vocab, 0)
+    assert e.value.code == nedo_gpu.ERR_ARG and "out of range" in str(e.value)
+    with pytest.raises(nedo_gpu.NedoGpuError) as e:
+        dec.forward(1, dec.cfg.context)
+    assert e.value.code == nedo_gpu.ERR_ARG
+
+
+def test_decoder_config_errors(cuda, tmp_path):
+    kw, prompt, max_new = M.MODELS["q8_gqa_window"]
+    p = str(tmp_path / "m.gguf")
+    G.synthetic_model(p, **kw)
+    g = G.GgufFile(p)
+    cfg = config_from_gguf(g)
+    lib = nedo_gpu.load()
+    bad = [("heads", 3, "invalid GQA dimensions"), ("context", 0, "context_length is zero"),
+           ("ffn", 256, "tensor shape does not match")]
+    for field, value, msg in bad:
+        c = config_from_gguf(g)
+        setattr(c, field, value)
+        with pytest.raises(nedo_gpu.NedoGpuError) as e:
+            Decoder(lib, c, _views(g, c))
+        assert msg in str(e.value), (field, str(e.value))
+    assert cfg.vocab == 512
+
+
+def _views(g, cfg):
+    # the tensor list Decoder.from_gguf builds, for a configuration edited by the test
+    names = ["token_embd.weight", "output_norm.weight", "output.weight", None]
+    for i in range(int(g.metadata["nedolm.block_count"])):
+        names += [f"blk.{i}.{k}.weight" for k in ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                                  "ffn_norm", "ffn_gate", "ffn_up", "ffn_down")]
+    out = []
+    for n in names:
+        v = nedo_gpu.TensorView()
+        if n is not None:
+            tt, shape, off, nb = g.tensors[n]
+            v.type, v.ndims = tt, len(shape)
+            for i, s in enumerate(shape):
+                v.shape[i] = s
+            v.data = g.buf[off:off + nb].ctypes.data
+            v.nbytes = nb
+        out.append(v)
+    return out
