@@ -27,6 +27,14 @@ Workloads (default q4_0_11008x4096):
                        plus an F16 64000x1536 head, for 1, 8 or 32 tokens per step
                        (the head takes the argmax at batch 1); GB/s with each
                        weight counted once per step, per-matrix GB/s in the line.
+  decode_forward_24x1536
+                       the device-resident decode forward pass of a NedoLM model
+                       with the sweep's matrices (nedo_gpu_decoder_*: norms, fused
+                       q|k|v and gate|up matvecs, RoPE, KV cache, attention, SiLU,
+                       head + argmax in one CUDA graph per pass), greedy generation
+                       with the loop on the device; GB/s of weights + KV cache per
+                       pass and tokens/s.  The reference arm runs the reference's
+                       own decode loop over the same GGUF.
 
 Timing: W warm-up steps, then exactly K steps between a barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max over
@@ -84,9 +92,16 @@ for _b in (1, 8, 32):
     WORKLOADS[f"decode_sweep_24x1536_b{_b}"] = dict(kind="sweep", type=B.Q8_0, layers=24, d=1536, ff=4096,
                                                     head=64000, batch=_b, shard="replica", argmax=_b == 1,
                                                     rows=1536, cols=1536)
+# the device-resident decode pass over the sweep's matrices: 12 heads x 128 with
+# 12 KV heads (so q/k/v are 1536x1536 as in the sweep), the F16 64000x1536 head
+# tied to the embedding, timed at positions 512.. of a running greedy decode
+WORKLOADS["decode_forward_24x1536"] = dict(kind="decoder", type=B.Q8_0, layers=24, d=1536, heads=12, kv_heads=12,
+                                           ff=4096, head=64000, context=4096, sliding=2048, pos=512, batch=1,
+                                           shard="replica", argmax=True, rows=1536, cols=1536)
 # measured beside the default line at N=1 (every configuration of the path)
 SIDE_WORKLOADS = ["q8_0_4096x4096", "f16_head_128000x2048", "q4_0_32768x32768", "q8_0_prefill_512x4096x14336",
-                  "decode_sweep_24x1536_b1", "decode_sweep_24x1536_b8", "decode_sweep_24x1536_b32"]
+                  "decode_sweep_24x1536_b1", "decode_sweep_24x1536_b8", "decode_sweep_24x1536_b32",
+                  "decode_forward_24x1536"]
 
 
 def sweep_matrices(wl):
@@ -168,6 +183,14 @@ def work_of(wl, rows_total, batch=None):
 
 def workload_config(name, wl, world):
     """The `config` of a line: identical in both arms (implementation details go to `setup`)."""
+    if wl.get("kind") == "decoder":
+        return {"workload": name,
+                "description": f"NedoLM decode forward pass, {wl['layers']} layers, d_model {wl['d']}, "
+                               f"{wl['heads']} heads x {wl['d'] // wl['heads']} ({wl['kv_heads']} KV heads), "
+                               f"FFN {wl['ff']}, Q8_0 projections, F16 {wl['head']}x{wl['d']} head tied to the "
+                               f"embedding, greedy, positions from {wl['pos']} (window {wl['sliding']})",
+                "batch": 1, "weight_bytes_per_step": decoder_bytes(wl, wl["pos"])["weights"],
+                "parallelism": "replicas" if world > 1 else "single"}
     if wl.get("kind") == "sweep":
         return {"workload": name,
                 "description": f"{wl['layers']}-layer d_model {wl['d']} decoder step: "
@@ -334,6 +357,16 @@ def check_sample(sample):
 def run_reference_arm(args, wl, world, rank):
     if rank != 0:
         return
+    if wl.get("kind") == "decoder":
+        cb = decoder_cpu(wl, budget_s=min(20.0, 0.05 * args.steps + 2.0))
+        line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic NedoLM GGUF (seeded weights)",
+                "config": workload_config(args.workload, wl, world),
+                "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                            "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if wl.get("kind") == "sweep":
         cb = sweep_cpu(wl, budget_s=min(20.0, 0.05 * args.steps + 2.0))
         line = {"metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference", "n_gpus": world,
@@ -377,6 +410,159 @@ def run_reference_arm(args, wl, world, rank):
         "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ decoder
+def decoder_bytes(wl, pos):
+    """Algorithmic bytes of one decode pass at `pos`: every weight once (the
+    embedding: one row), the KV cache rows attention reads and the new ones."""
+    d, ff, L = wl["d"], wl["ff"], wl["layers"]
+    hd = d // wl["heads"]
+    qd, kvd = wl["heads"] * hd, wl["kv_heads"] * hd
+    rb = B.row_bytes
+    t = wl["type"]
+    layer = (qd + 2 * kvd) * rb(t, d) + d * rb(t, qd) + 2 * ff * rb(t, d) + d * rb(t, ff) + 2 * 4 * d
+    weights = L * layer + wl["head"] * 2 * d + 4 * d + 2 * d
+    window = min(wl["sliding"] or wl["context"], wl["context"])
+    nctx = min(pos + 1, window)
+    kv = L * (nctx + 1) * kvd * 4 * 2
+    return {"weights": weights, "kv": kv, "total": weights + kv}
+
+
+_DECODER_FILE = {}
+
+
+def decoder_model(wl):
+    """Path of the synthetic GGUF of the decoder workload (built once per process)."""
+    key = id(wl)
+    if key not in _DECODER_FILE:
+        from nedo_gpu import gguf as G
+
+        path = os.path.join(tempfile.mkdtemp(prefix="nedo_bench_"), "decoder.gguf")
+        G.synthetic_model(path, dim=wl["d"], layers=wl["layers"], heads=wl["heads"], kv_heads=wl["kv_heads"],
+                          ffn=wl["ff"], vocab=wl["head"], context=wl["context"], sliding=wl["sliding"],
+                          wtype=wl["type"], emb_type=B.F16, tied=True, norm_type=0, shared_layers=True, seed=5)
+        _DECODER_FILE[key] = path
+    return _DECODER_FILE[key]
+
+
+REF_DECODE = os.path.join(ROOT, "oracle", "_ref", "ref_decode")
+
+
+def ref_decode_run(path, prompt, max_new, logits=True):
+    """(seconds, logits [passes, vocab] or None, ids) of the reference's own decode
+    loop (oracle/_ref/ref_decode: src/model.cpp generate_ids, greedy)."""
+    out = os.path.join(tempfile.mkdtemp(prefix="nedo_ref_"), "out.bin")
+    env = dict(os.environ, OMP_NUM_THREADS=str(host_cores()))
+    t0 = time.perf_counter()
+    subprocess.run([REF_DECODE, path, out, str(max_new), "0", "0", "0", "0"] + [str(t) for t in prompt],
+                   check=True, env=env, stdout=subprocess.DEVNULL)
+    sec = time.perf_counter() - t0
+    b = open(out, "rb").read()
+    a = np.frombuffer(b, dtype=np.uint32)
+    steps, vocab = int(a[0]), int(a[1])
+    lg = np.frombuffer(b, dtype=np.float32, count=steps * vocab, offset=8).reshape(steps, vocab) if logits else None
+    n = int(a[2 + steps * vocab])
+    return sec, lg, [int(v) for v in a[3 + steps * vocab:3 + steps * vocab + n]]
+
+
+def decoder_cpu(wl, budget_s=10.0):
+    """The reference's decode loop on this host: seconds per pass from two runs
+    (one pass, then 1 + m passes) so the model load cancels."""
+    if not os.path.exists(REF_DECODE):
+        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/ref_decode not built (make -C oracle ref)"}
+    path = decoder_model(wl)
+    t1, _, _ = ref_decode_run(path, [5], 0, logits=False)
+    m = 8
+    tm, _, _ = ref_decode_run(path, [5], m, logits=False)
+    per = max((tm - t1) / m, 1e-6)
+    m = int(min(max(8, budget_s / per), 256))
+    tm, _, ids = ref_decode_run(path, [5], m, logits=False)
+    t1, _, _ = ref_decode_run(path, [5], 0, logits=False)
+    passes = len(ids)  # passes after the first: one per generated id (eos may stop it early)
+    per = max((tm - t1) / max(passes, 1), 1e-6)
+    byts = decoder_bytes(wl, passes // 2)["total"]
+    return {"value": round(byts / per / 1e9, 3), "unit": "GB/s", "cores": host_cores(), "kind": "reference",
+            "tokens_per_s": round(1.0 / per, 2),
+            "sample": f"the reference's generate_ids (oracle/_ref/ref_decode) over the same GGUF: {passes} greedy "
+                      f"passes at positions 1..{passes} ({per * 1e3:.2f} ms each), the one-pass run subtracted"}
+
+
+def measure_decoder(ctx, name, steps, keep_sample=False):
+    """The device-resident decode pass: greedy generation with the loop on the
+    device, `steps` passes at positions wl['pos'].. after filling the KV cache."""
+    torch, lib = ctx.torch, ctx.lib
+    from nedo_gpu import gguf as G
+    from nedo_gpu.decoder import Decoder
+
+    wl = WORKLOADS[name]
+    g = G.GgufFile(decoder_model(wl))
+    dec = Decoder.from_gguf(g, lib)
+    dec.set_stream(ctx.stream.cuda_stream)
+    p0 = wl["pos"]
+    steps = max(1, min(steps, wl["context"] - p0 - 1, 200))
+    ids = dec.generate(5, 0, p0)  # positions 0 .. p0-1: the cache the timed passes attend over
+    tok = ids[-1]
+    sampler = ClockSampler(ctx.local_rank)
+    sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    while time.perf_counter() < soak_end:
+        dec.generate(tok, p0, steps)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    ev0.record(ctx.stream)
+    gen = dec.generate(tok, p0, steps)
+    ev1.record(ctx.stream)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ms = ctx.max_over_ranks(ev0.elapsed_time(ev1)) / steps
+    clocks = sampler.stop()
+    byts = decoder_bytes(wl, p0 + steps // 2)
+    value = byts["total"] / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    # e2e: the same passes as host calls (token in, greedy id out, one round trip each)
+    t0 = time.perf_counter()
+    t = tok
+    for k in range(steps):
+        t, _ = dec.forward(t, p0 + k, logits=False)
+    e2e_sec = ctx.max_over_ranks(time.perf_counter() - t0) / steps
+    mats = 4 * wl["layers"] + 1
+    out = {"value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 6), "steps": steps,
+           "tokens_per_s": round(1e3 / ms, 2), "launches_per_step": 3 + 5 * wl["layers"] + 1,
+           "matvecs_per_step": mats,
+           "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(value / peak, 4), "traffic": None, "peak_source": peak_kind,
+                        "launch_us": round(ms * 1e3, 3), "bytes_per_step": byts},
+           "clocks": clocks,
+           "e2e": {"value": round(byts["total"] / e2e_sec / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 16,
+                   "d2h_bytes_per_step": 12 + 16, "ms_per_step": round(e2e_sec * 1e3, 4),
+                   "tokens_per_s": round(1.0 / e2e_sec, 2),
+                   "path": "nedo_gpu_decoder_forward per token (token id in, greedy id out)"},
+           "generated": gen[:8]}
+    if keep_sample:
+        out["parity"] = decoder_parity(dec, wl)
+    dec.close()
+    g.close()
+    return out
+
+
+def decoder_parity(dec, wl, prompt=(5, 300, 301, 302), tol=2e-4):
+    """Checker of the CPU baseline leg: the decoder's logits on a short sequence
+    against the reference's own decode loop on the same GGUF."""
+    if not os.path.exists(REF_DECODE):
+        return {"ok": None, "checker": "unavailable: oracle/_ref/ref_decode not built"}
+    _, ref, _ = ref_decode_run(decoder_model(wl), list(prompt), 0)
+    dec.reset()
+    worst, same = 0.0, True
+    for pos, t in enumerate(prompt):
+        pick, lg = dec.forward(t, pos)
+        worst = max(worst, float(np.abs(lg - ref[pos]).max() / np.abs(ref[pos]).max()))
+        same = same and pick == int(np.argmax(ref[pos]))
+    return {"ok": bool(worst <= tol and same), "max_logit_err_over_max_logit": worst, "tolerance": tol,
+            "argmax_equal": same, "checker": "reference decode loop (oracle/_ref/ref_decode)",
+            "checked": f"{len(prompt)} passes, logits of each"}
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -625,7 +811,8 @@ def measure_sweep(ctx, name, steps_req, keep_sample=False):
 
 
 def side_record(r):
-    keep = ("value", "unit", "ms_per_step", "roofline", "clocks", "parity", "per_matrix", "launches_per_step")
+    keep = ("value", "unit", "ms_per_step", "roofline", "clocks", "parity", "per_matrix", "launches_per_step",
+            "tokens_per_s", "e2e")
     return {k: r[k] for k in keep if k in r}
 
 
@@ -815,6 +1002,24 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
     name = args.workload
     check = rank == 0 and world == 1 and not args.no_cpu_baseline
     setup = {}
+    if wl.get("kind") == "decoder":
+        r = measure_decoder(ctx, name, args.steps, keep_sample=check)
+        line = {"metric": METRIC, "value": round(r["value"] * world, 2), "unit": "GB/s", "n_gpus": world,
+                "steps": r["steps"], "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+f32",
+                "data": "synthetic NedoLM GGUF (seeded weights, layers sharing one set of bytes)",
+                "config": workload_config(name, wl, world),
+                "setup": {"l2": "918 MB of weights resident: each pass streams them from HBM (> 4x L2)",
+                          "graph": "one CUDA graph per pass (3 + 5 x layers launches: norms and SiLU fused into the projections; + the on-device advance)",
+                          "pdl": True, "tokens_per_s": r["tokens_per_s"]},
+                "roofline": r["roofline"], "e2e": r["e2e"], "gpu_launches": r["steps"] * r["launches_per_step"],
+                "clocks": r["clocks"]}
+        if check:
+            line["cpu_baseline"] = decoder_cpu(wl)
+            line["parity"] = r["parity"]
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     if wl.get("kind") == "sweep":
         r = measure_sweep(ctx, name, args.steps, keep_sample=check)
         e2e = e2e_sweep(ctx, wl, r["_state"])
@@ -902,9 +1107,13 @@ def run_gpu_arm(args, wl, world, rank, local_rank):
                 continue
             torch.cuda.empty_cache()
             ow = WORKLOADS[other]
-            rr = (measure_sweep(ctx, other, 20, keep_sample=check) if ow.get("kind") == "sweep" else
-                  measure_matvec(ctx, other, 20 if batch_of(ow) == 1 else 10, keep_sample=check))
-            if check:
+            if ow.get("kind") == "decoder":
+                rr = measure_decoder(ctx, other, 50, keep_sample=check)
+            elif ow.get("kind") == "sweep":
+                rr = measure_sweep(ctx, other, 20, keep_sample=check)
+            else:
+                rr = measure_matvec(ctx, other, 20 if batch_of(ow) == 1 else 10, keep_sample=check)
+            if check and "sample" in rr:
                 rr["parity"] = check_sample(rr.pop("sample"))
             side[other] = side_record(rr)
             del rr

@@ -323,6 +323,21 @@ NEDO_GPU_API int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, con
 NEDO_GPU_API int nedo_gpu_decoder_forward(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, float* logits_host,
                                           uint32_t* argmax_out);
 
+/* Greedy generation with the loop on the device: n passes, the first for
+ * `token` at `pos`, each next pass fed the previous pass's greedy pick; the
+ * picks go to ids_host[0..n) (ids_host[k] is the pick of pass k).  Equivalent
+ * to n forward calls with temperature-0 sampling between them
+ * (src/model.cpp:271-279) but without a host round trip per token: the n
+ * passes are launched back to back and the ids read once.  The eos id does
+ * not stop the device loop (the caller truncates at it); pos + n <= context. */
+NEDO_GPU_API int nedo_gpu_decoder_generate(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, uint32_t n,
+                                           uint32_t* ids_host);
+
+/* Run the passes on `stream` (a cudaStream_t; NULL returns to the decoder's
+ * own stream).  The captured graphs are dropped and captured again on the
+ * next calls.  Every forward call still waits for its pass to finish. */
+NEDO_GPU_API int nedo_gpu_decoder_set_stream(nedo_gpu_decoder* d, void* stream);
+
 /* The logits of the last forward pass in device memory (valid until the next
  * call), for the sampler entry points (nedo_gpu_topk_dev). */
 NEDO_GPU_API int nedo_gpu_decoder_logits_dev(nedo_gpu_decoder* d, const float** logits_dev);

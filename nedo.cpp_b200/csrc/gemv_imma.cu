@@ -98,6 +98,7 @@ struct ImmaArgs {
     uint64_t peer_row_offset;
     float* peer_y[kMaxPeers];
     uint32_t* peer_signal[kMaxPeers];
+    XPrologue pro;  // slice kernel only
 };
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -644,11 +645,14 @@ __global__ void __maxnreg__(NT == 1 ? 96 : 128)
 // Streaming.  Copy units are wide (16 rows x UP block pairs, about 1.1 KB per
 // row): the tensor-map engine's cost grows with the number of box rows, and
 // units this wide stream a 25 MB matrix at the HBM rate where 0.5 KB rows do
-// not.  At CTA start (before griddepcontrol.wait) the producer asks L2 to
-// prefetch the whole slice; the copies into shared memory are issued only
-// after every consumer warp has issued its loads of x, so that x (needed first)
-// is not queued behind this SM's weight stream.  Copies go out chunk-major
-// (chunk 0 of every tile first), the order the compute consumes them.
+// not.  The first copies (about as much as lands while the CTA waits for the
+// previous kernel) are issued at CTA start, before griddepcontrol.wait; the
+// rest only after every consumer warp has issued its loads of x, so that x
+// (needed first) is not queued behind this SM's whole weight stream.  Copies
+// go out chunk-major (chunk 0 of every tile first), the order the compute
+// consumes them.  The next kernel on the stream is released
+// (griddepcontrol.launch_dependents) once this CTA is past its dependency
+// wait, so at most one kernel's CTAs wait behind a running one.
 //
 // Compute.  A work item is one sub-segment of kSubPairs block pairs of up to R
 // consecutive tiles: the x side of each pair (B registers, column scales,
@@ -756,7 +760,10 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
     // [partial sums: tiles_cap x nsub x 16][full: slots][x requested][abort flag]
     uint8_t* table = smem + static_cast<size_t>(a.slots) * a.unit_bytes;
     float* part = reinterpret_cast<float*>(table + static_cast<size_t>(a.group_pairs) * kPairTableBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(part + static_cast<size_t>(tiles_cap) * nsub * 16u);
+    // (at least 2 * W floats: the prologue's partial sums of squares use them first)
+    const size_t part_floats = static_cast<size_t>(tiles_cap) * nsub * 16u > 2u * W ? static_cast<size_t>(tiles_cap) * nsub * 16u
+                                                                                    : 2u * W;
+    uint64_t* full = reinterpret_cast<uint64_t*>(part + part_floats);
     uint64_t* xbar = full + a.slots;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(xbar + 1);
 
@@ -768,7 +775,6 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
     }
     __syncwarp();
     __syncthreads();
-    grid_launch_dependents();
 
     if (warp == W) {
         // producer (one thread)
@@ -779,7 +785,12 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
         for (uint32_t c = 0; c < nchunk && ok; ++c) {
             // the first early_chunks chunks stream during griddepcontrol.wait; the rest
             // once every consumer warp has issued its x loads
-            if (c == a.early_chunks) ok = mbar_wait_bounded(xbar, 0u, a.status, 24u);
+            if (c == a.early_chunks) {
+                ok = mbar_wait_bounded(xbar, 0u, a.status, 24u);
+                // every consumer warp is past griddepcontrol.wait: the next kernel may be
+                // scheduled now (not earlier, so that at most one kernel waits behind this one)
+                grid_launch_dependents();
+            }
             if (!ok) break;
             for (uint32_t t = 0; t < my_tiles; ++t, ++issued) {
                 const uint32_t u = t * nchunk + c;
@@ -789,6 +800,10 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
                                  static_cast<int32_t>(c * UP * pb / 8u),
                                  static_cast<int32_t>((tile_begin + t) * kTileRows), &full[u], policy);
             }
+        }
+        if (a.early_chunks >= nchunk) {
+            ok = mbar_wait_bounded(xbar, 0u, a.status, 24u) && ok;
+            grid_launch_dependents();
         }
         if (!ok) *abort_flag = 1u;
         // every issued copy lands before the CTA may exit
@@ -805,19 +820,102 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
     const size_t off_b = off_a + 8u * static_cast<size_t>(a.box_bytes);
 
     grid_dependency_wait();  // x may come from the previous kernel
+    grid_launch_dependents();
     {
         // the x limb table: every x load issued, the producer released, then the limbs
         const uint32_t tid = threadIdx.x, per_pass = W * 32u / 8u, q = tid & 7u;
         const uint32_t blocks = 2u * a.pairs_total;  // at most per_pass * kLimbPasses (planned)
-        float4 v[kLimbPasses];
+        const XPrologue& pro = a.pro;
+        float4 v[kLimbPasses], v2[kLimbPasses];
 #pragma unroll
         for (uint32_t k = 0; k < kLimbPasses; ++k) {
             const uint32_t f = k * per_pass + tid / 8u;
-            v[k] = f < blocks ? __ldg(reinterpret_cast<const float4*>(a.x + 32u * f + 4u * q))
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            const size_t e = 32u * f + 4u * q;
+            v[k] = f < blocks ? __ldg(reinterpret_cast<const float4*>(a.x + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            // the second operand of the prologue: delta (norm) or up (silu)
+            const float* second = pro.mode == kPrologueNorm ? pro.delta : pro.mode == kPrologueSilu ? pro.up : nullptr;
+            v2[k] = (f < blocks && second) ? __ldg(reinterpret_cast<const float4*>(second + e))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            // the norm weight is read after the sum of squares: bring its line into L1
+            // now, so that read does not queue behind this SM's weight copies
+            if (pro.mode == kPrologueNorm && f < blocks && q == 0) {
+                const void* wl = pro.wtype == 0 ? static_cast<const void*>(static_cast<const float*>(pro.w) + 32u * f)
+                                                : static_cast<const void*>(static_cast<const uint16_t*>(pro.w) + 32u * f);
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(wl));
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(xbar);
+        if (pro.mode == kPrologueNorm) {
+            // x + delta, its sum of squares in double (each CTA the same, in a fixed order)
+            double ss = 0.0;
+#pragma unroll
+            for (uint32_t k = 0; k < kLimbPasses; ++k) {
+                const uint32_t f = k * per_pass + tid / 8u;
+                if (f >= blocks) continue;
+                float4& x4 = v[k];
+                x4.x += v2[k].x;
+                x4.y += v2[k].y;
+                x4.z += v2[k].z;
+                x4.w += v2[k].w;
+                if (pro.x_out && blockIdx.x == 0)
+                    *reinterpret_cast<float4*>(pro.x_out + 32u * f + 4u * q) = x4;
+                ss += static_cast<double>(x4.x) * x4.x;
+                ss += static_cast<double>(x4.y) * x4.y;
+                ss += static_cast<double>(x4.z) * x4.z;
+                ss += static_cast<double>(x4.w) * x4.w;
+            }
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+            double* red = reinterpret_cast<double*>(part);  // free until the items write their sums
+            if (lane == 0) red[warp] = ss;
+            named_barrier_sync(1, W * 32u);
+            double tot = 0.0;
+            for (uint32_t i = 0; i < W; ++i) tot += red[i];
+            const uint32_t n = 64u * a.pairs_total;
+            const float inv = 1.0f / sqrtf(static_cast<float>(tot / n) + pro.eps);
+#pragma unroll
+            for (uint32_t k = 0; k < kLimbPasses; ++k) {
+                const uint32_t f = k * per_pass + tid / 8u;
+                if (f >= blocks) continue;
+                const size_t e = 32u * f + 4u * q;
+                float4 w4;
+                if (pro.wtype == 0) {
+                    w4 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(pro.w) + e));
+                } else {
+                    const uint2 hb = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(pro.w) + e));
+                    w4 = make_float4(half_bits_to_float(hb.x & 0xFFFFu), half_bits_to_float(hb.x >> 16),
+                                     half_bits_to_float(hb.y & 0xFFFFu), half_bits_to_float(hb.y >> 16));
+                }
+                v[k].x = v[k].x * inv * w4.x;
+                v[k].y = v[k].y * inv * w4.y;
+                v[k].z = v[k].z * inv * w4.z;
+                v[k].w = v[k].w * inv * w4.w;
+            }
+            named_barrier_sync(1, W * 32u);  // every warp has read the partial sums
+        } else if (pro.mode == kPrologueSilu) {
+            bool mask_root = false, mask_suffix = false;
+            if (pro.route) {
+                const uint32_t tok = pro.io->token;
+                mask_root = pro.route[2u * tok] < 0.5f;
+                mask_suffix = pro.route[2u * tok + 1u] < 0.5f;
+            }
+            const uint32_t r0 = pro.m_shared, r1 = r0 + pro.m_root, r2 = r1 + pro.m_suffix;
+#pragma unroll
+            for (uint32_t k = 0; k < kLimbPasses; ++k) {
+                const uint32_t f = k * per_pass + tid / 8u;
+                if (f >= blocks) continue;
+                const uint32_t e = 32u * f + 4u * q;
+                float* g = reinterpret_cast<float*>(&v[k]);
+                const float* u = reinterpret_cast<const float*>(&v2[k]);
+#pragma unroll
+                for (uint32_t c = 0; c < 4; ++c) {
+                    float o = (g[c] / (1.0f + expf(-g[c]))) * u[c];
+                    const uint32_t i = e + c;
+                    if (pro.route && ((mask_root && i >= r0 && i < r1) || (mask_suffix && i >= r1 && i < r2))) o = 0.f;
+                    g[c] = o;
+                }
+            }
+        }
 #pragma unroll
         for (uint32_t k = 0; k < kLimbPasses; k += 2) {
             // the 8 threads of a block share f (the shuffles inside span exactly them)
@@ -1044,7 +1142,8 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
         const uint64_t slots = tiles_per_cta * nchunk;
         const uint64_t unit = kTileRows * box;
         const uint64_t nsub = (pairs_total + kSubPairs - 1) / kSubPairs;
-        const uint64_t smem = slots * unit + pairs_total * kPairTableBytes + tiles_per_cta * nsub * 64u + 8u * slots + 32u;
+        const uint64_t part_floats = tiles_per_cta * nsub * 16u > 2u * kMaxWarps ? tiles_per_cta * nsub * 16u : 2u * kMaxWarps;
+        const uint64_t smem = slots * unit + pairs_total * kPairTableBytes + part_floats * 4u + 8u * slots + 32u;
         // the x table's blocks in one pass of the consumer threads' registers
         if (box <= kMaxBoxBytes && smem <= budget && 2u * pairs_total <= kMaxWarps * 4u * kLimbPasses) {
             p.type = type;
@@ -1145,7 +1244,8 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
 
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather, uint64_t ldx,
-                        uint64_t ldy) {
+                        uint64_t ldy, const XPrologue* prologue) {
+    if (prologue && prologue->mode != kPrologueNone && !plan.slice) return cudaErrorInvalidValue;
     if (!plan.ok || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
         return cudaErrorInvalidValue;
     if (ldx == 0) ldx = cols;
@@ -1190,6 +1290,7 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
     a.ldy = ldy;
     a.status = status;
     a.early_chunks = plan.early_chunks;
+    if (prologue) a.pro = *prologue;
     if (plan.slice) {
         if (plan.type == kQ8_0) return launch_slice_p<kQ8_0>(plan, map, a, stream, pdl);
         return launch_slice_p<kQ4_0>(plan, map, a, stream, pdl);

@@ -104,9 +104,29 @@ struct PeerGather {
 };
 // plan.tokens token vectors: x [tokens][ldx], y [tokens][ldy] (0 = cols / rows);
 // every weight unit is read once for all of them.
+// The input transform a resident-slice launch (plan.slice) can apply to x as
+// it builds its x table, fusing the step that precedes a projection in the
+// decode pass: kPrologueNorm x_in = RMSNorm(x + delta) * w (src/kernels.cpp:50-72;
+// every CTA sums the squares itself, CTA 0 also stores x + delta to x_out),
+// kPrologueSilu x_in = silu(x) * up with the MorphFFN masking
+// (src/kernels.cpp:88-91, src/model.cpp:196-209).
+enum : uint32_t { kPrologueNone = 0, kPrologueNorm = 1, kPrologueSilu = 2 };
+struct DecodeIo;
+struct XPrologue {
+    uint32_t mode = kPrologueNone;
+    const float* delta = nullptr;  // norm: added to x first (may be null)
+    const void* w = nullptr;       // norm: weight (F32 or F16)
+    uint32_t wtype = 0;            // 0 F32, 1 F16
+    float eps = 0.f;
+    float* x_out = nullptr;        // norm: x + delta (may be null)
+    const float* up = nullptr;     // silu: the up half
+    const float* route = nullptr;  // silu: MorphFFN flags [vocab][2] (null: no masking)
+    const DecodeIo* io = nullptr;  // silu with route: the token
+    uint32_t m_shared = 0, m_root = 0, m_suffix = 0;
+};
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr,
-                        uint64_t ldx = 0, uint64_t ldy = 0);
+                        uint64_t ldx = 0, uint64_t ldy = 0, const XPrologue* prologue = nullptr);
 
 // Batch-1 Q8_0 / Q4_0 on tcgen05 (kind::i8, A from TMEM): 16-row tiles, one
 // MMA per 8 blocks of a tile (M = 16 rows x 8 blocks), at most ~110 KB of
@@ -191,7 +211,7 @@ uint64_t row_bytes_of(uint32_t type, uint64_t cols);
 struct DecodeIo {
     uint64_t pos;
     uint32_t token;
-    uint32_t pad;
+    uint32_t step;  // generation: passes run so far (index of the next pick in ids)
 };
 // x = embedding row io->token (F16 / Q8_0 / Q4_0 rows of `cols`; an id >= rows sets kErrArgument).
 cudaError_t launch_embed(uint32_t type, const void* w, uint64_t cols, uint64_t rows, const DecodeIo* io, float* x,
@@ -199,13 +219,16 @@ cudaError_t launch_embed(uint32_t type, const void* w, uint64_t cols, uint64_t r
 // x += delta (delta may be null), y = RMSNorm(x) * w (w F32, wtype 0, or F16, wtype 1).
 cudaError_t launch_add_rmsnorm(float* x, const float* delta, const void* w, uint32_t wtype, float* y, uint32_t n,
                                float eps, cudaStream_t stream, bool pdl);
-// RoPE on q and k of qkv = [q (nq x hd) | k (nkv x hd) | v (nkv x hd)], k and v into slot io->pos % window.
-cudaError_t launch_rope_kv(float* qkv, uint32_t nq, uint32_t nkv, uint32_t hd, float theta, const DecodeIo* io,
-                           float* kcache, float* vcache, uint32_t window, cudaStream_t stream, bool pdl);
-size_t attention_smem_bytes(uint32_t window, uint32_t hd);
-cudaError_t launch_attention(const float* qkv, const float* kcache, const float* vcache, float* att,
-                             const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd, uint32_t window,
-                             float inv_sqrt_hd, cudaStream_t stream, bool pdl);
+// RoPE, the KV-cache write of position io->pos and attention of the nq heads
+// over the window, for qkv = [q (nq x hd) | k (nkv x hd) | v (nkv x hd)]: one
+// launch of attention_splits(window) x nq CTAs; part holds nq x splits x
+// (hd + 2) floats, counter nq zeros (left zero).
+uint32_t attention_splits(uint32_t window);
+cudaError_t launch_attention(const float* qkv, float* kcache, float* vcache, float* att, float* part,
+                             uint32_t* counter, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
+                             uint32_t window, float theta, float inv_sqrt_hd, cudaStream_t stream, bool pdl);
+// io->token = pick, io->pos += 1, ids[io->step++] = pick (single thread, after the pass).
+cudaError_t launch_advance(DecodeIo* io, const int64_t* pick, uint32_t* ids, uint32_t cap, cudaStream_t stream);
 // gu = [gate | up] (f each): gate = silu(gate) * up, MorphFFN masks when route is non-null.
 cudaError_t launch_silu_mul(float* gu, uint32_t f, const float* route, const DecodeIo* io, uint32_t shared_w,
                             uint32_t root_w, uint32_t suffix_w, cudaStream_t stream, bool pdl);

@@ -16,6 +16,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
 #include <vector>
 
 #include "../../include/nedo_gpu.h"
@@ -981,7 +982,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
 // or triple that shares its input is one matvec launch (rows concatenated, row
 // bytes unchanged); the fp32 KV cache [layer][window][kv_heads * head_dim] for
 // keys and for values; fp32 activations x, xn, qkv, att, tmp, gu and the logits.
-// A pass is 2 + 9 * layers launches on one stream (programmatic dependent
+// A pass is 3 + 5 * layers launches on one stream (3 + 8 * layers where the
+// norms and the SiLU gate cannot be fused into the projections) (programmatic dependent
 // launch between them), captured once as a CUDA graph that also uploads the
 // token and position and downloads the greedy pick and the status word.
 namespace {
@@ -989,7 +991,27 @@ namespace {
 struct DecLayer {
     uint32_t an_type = 0, fn_type = 0, qkv_type = 0, o_type = 0, gu_type = 0, down_type = 0;
     const void *an = nullptr, *fn = nullptr, *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+    // the projection runs the resident-slice int8 kernel with the preceding
+    // RMSNorm (qkv, gu) or SiLU gate (down) fused into its x-table build
+    bool qkv_fused = false, gu_fused = false, down_fused = false;
 };
+
+// A projection with its input transform fused (XPrologue), on the resident-slice plan.
+int matvec_fused(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x, float* y,
+                 const XPrologue& pro, cudaStream_t stream) {
+    ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+    if (!ip.ok || !ip.slice) return fail(NEDO_GPU_ERR_ARG, "fused projection without a resident-slice plan");
+    cudaError_t e = launch_imma(ip, w, x, y, rows, cols, s->status, stream, true, nullptr, 0, 0, &pro);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_imma (fused) launch");
+    return 0;
+}
+
+bool fusable(const DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols) {
+    if (type != kQ8_0 && type != kQ4_0) return false;
+    if (tc8_enabled()) return false;  // the opt-in tcgen05 kernel takes these shapes instead
+    const ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem);
+    return ip.ok && ip.slice;
+}
 
 struct DecPin {
     DecodeIo io;
@@ -1011,16 +1033,21 @@ struct nedo_gpu_decoder {
     const float* route = nullptr;
     std::vector<DecLayer> layers;
     std::vector<void*> owned;
-    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *tmp = nullptr, *gu = nullptr;
+    float *x = nullptr, *x2 = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *tmp = nullptr, *gu = nullptr;
     float *logits = nullptr, *kcache = nullptr, *vcache = nullptr;
+    float* attn_part = nullptr;  // attention split partials [heads][splits][head_dim + 2]
+    uint32_t* attn_counter = nullptr;  // [heads] finished splits (reset by the combining CTA)
     DecodeIo* io = nullptr;
     int64_t* amax = nullptr;  // index, then the value (float) in the next 8 bytes
     ArgmaxScratch scratch{};
     DecPin* pin = nullptr;
     float* logits_pin = nullptr;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;      // the stream the passes run on
+    cudaStream_t own_stream = nullptr;  // created with the decoder
     cudaGraphExec_t graph[2] = {nullptr, nullptr};  // without / with the logits download
     bool eager_done[2] = {false, false};
+    cudaGraphExec_t gen_graph = nullptr;  // one pass + the on-device advance (generation)
+    uint32_t* ids = nullptr;              // [context] picks of a generation
 };
 
 namespace {
@@ -1089,34 +1116,64 @@ int dec_enqueue(nedo_gpu_decoder* d) {
     cudaError_t e = launch_embed(d->emb_type, d->emb, c.dim, d->emb_rows, d->io, d->x, s->status, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "embedding launch");
     const size_t cache_layer = static_cast<size_t>(d->window) * d->kvd;
+    // the residual stream lives in xcur; a fused norm writes x + delta to the
+    // other buffer (CTA 0 of the projection), so the two alternate
+    float* xcur = d->x;
+    float* xalt = d->x2;
+    const float* pending = nullptr;  // a residual not yet added to xcur
+    auto norm_into = [&](bool fused, const void* nw, uint32_t nwt, uint32_t type, uint64_t rows, const void* w,
+                         float* y) -> int {
+        if (fused) {
+            XPrologue pro;
+            pro.mode = kPrologueNorm;
+            pro.delta = pending;
+            pro.w = nw;
+            pro.wtype = nwt == 0 ? 0u : 1u;
+            pro.eps = c.rms_eps;
+            pro.x_out = xalt;
+            if (int rc = matvec_fused(s, type, rows, c.dim, w, xcur, y, pro, st)) return rc;
+            std::swap(xcur, xalt);
+        } else {
+            cudaError_t ee = launch_add_rmsnorm(xcur, pending, nw, nwt == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps, st, pdl);
+            if (ee != cudaSuccess) return cuda_fail(ee, "rmsnorm launch");
+            if (int rc = dispatch_matvec(s, type, rows, c.dim, w, d->xn, y, 1, nullptr, st, 1)) return rc;
+        }
+        pending = nullptr;
+        return 0;
+    };
     for (uint32_t li = 0; li < c.layers; ++li) {
         const DecLayer& L = d->layers[li];
-        e = launch_add_rmsnorm(d->x, li ? d->tmp : nullptr, L.an, L.an_type == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps,
-                               st, pdl);
-        if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
-        if (int rc = dispatch_matvec(s, L.qkv_type, d->qd + 2u * d->kvd, c.dim, L.qkv, d->xn, d->qkv, 1, nullptr, st, 1))
-            return rc;
+        if (int rc = norm_into(L.qkv_fused, L.an, L.an_type, L.qkv_type, d->qd + 2u * d->kvd, L.qkv, d->qkv)) return rc;
         float* kc = d->kcache + li * cache_layer;
         float* vc = d->vcache + li * cache_layer;
-        e = launch_rope_kv(d->qkv, c.heads, c.kv_heads, hd, c.rope_theta, d->io, kc, vc, d->window, st, pdl);
-        if (e != cudaSuccess) return cuda_fail(e, "rope launch");
-        e = launch_attention(d->qkv, kc, vc, d->att, d->io, c.heads, c.kv_heads, hd, d->window, inv_sqrt_hd, st, pdl);
+        e = launch_attention(d->qkv, kc, vc, d->att, d->attn_part, d->attn_counter, d->io, c.heads, c.kv_heads, hd,
+                             d->window, c.rope_theta, inv_sqrt_hd, st, pdl);
         if (e != cudaSuccess) return cuda_fail(e, "attention launch");
         if (int rc = dispatch_matvec(s, L.o_type, c.dim, d->qd, L.o, d->att, d->tmp, 1, nullptr, st, 1)) return rc;
-        e = launch_add_rmsnorm(d->x, d->tmp, L.fn, L.fn_type == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps, st, pdl);
-        if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
-        if (int rc = dispatch_matvec(s, L.gu_type, 2u * c.ffn, c.dim, L.gu, d->xn, d->gu, 1, nullptr, st, 1))
-            return rc;
+        pending = d->tmp;
+        if (int rc = norm_into(L.gu_fused, L.fn, L.fn_type, L.gu_type, 2u * c.ffn, L.gu, d->gu)) return rc;
         // MorphFFN occupies the trailing morph_layers blocks (src/model.cpp:200)
         const bool morph = d->route != nullptr && li + c.morph_layers >= c.layers;
-        e = launch_silu_mul(d->gu, c.ffn, morph ? d->route : nullptr, d->io, c.morph_shared, c.morph_root,
-                            c.morph_suffix, st, pdl);
-        if (e != cudaSuccess) return cuda_fail(e, "silu launch");
-        if (int rc = dispatch_matvec(s, L.down_type, c.dim, c.ffn, L.down, d->gu, d->tmp, 1, nullptr, st, 1))
-            return rc;
+        if (L.down_fused) {
+            XPrologue pro;
+            pro.mode = kPrologueSilu;
+            pro.up = d->gu + c.ffn;
+            pro.route = morph ? d->route : nullptr;
+            pro.io = d->io;
+            pro.m_shared = c.morph_shared;
+            pro.m_root = c.morph_root;
+            pro.m_suffix = c.morph_suffix;
+            if (int rc = matvec_fused(s, L.down_type, c.dim, c.ffn, L.down, d->gu, d->tmp, pro, st)) return rc;
+        } else {
+            e = launch_silu_mul(d->gu, c.ffn, morph ? d->route : nullptr, d->io, c.morph_shared, c.morph_root,
+                                c.morph_suffix, st, pdl);
+            if (e != cudaSuccess) return cuda_fail(e, "silu launch");
+            if (int rc = dispatch_matvec(s, L.down_type, c.dim, c.ffn, L.down, d->gu, d->tmp, 1, nullptr, st, 1))
+                return rc;
+        }
+        pending = d->tmp;
     }
-    e = launch_add_rmsnorm(d->x, c.layers ? d->tmp : nullptr, d->onorm, d->onorm_type == 0 ? 0u : 1u, d->xn, c.dim,
-                           c.rms_eps, st, pdl);
+    e = launch_add_rmsnorm(xcur, pending, d->onorm, d->onorm_type == 0 ? 0u : 1u, d->xn, c.dim, c.rms_eps, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
     ArgmaxScratch a = d->scratch;
     a.out_index = d->amax;
@@ -1141,11 +1198,12 @@ int dec_step_ops(nedo_gpu_decoder* d, bool with_logits) {
 void dec_free(nedo_gpu_decoder* d) {
     for (auto& g : d->graph)
         if (g) cudaGraphExecDestroy(g);
+    if (d->gen_graph) cudaGraphExecDestroy(d->gen_graph);
     if (d->stream) cudaStreamSynchronize(d->stream);
     for (void* p : d->owned) cudaFree(p);
     if (d->pin) cudaFreeHost(d->pin);
     if (d->logits_pin) cudaFreeHost(d->logits_pin);
-    if (d->stream) cudaStreamDestroy(d->stream);
+    if (d->own_stream) cudaStreamDestroy(d->own_stream);
     delete d;
 }
 
@@ -1173,8 +1231,9 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
     if (!c.heads || !c.kv_heads || c.heads % c.kv_heads || c.dim != c.heads * c.head_dim)
         return fail(NEDO_GPU_ERR_ARG, "invalid GQA dimensions");
     if (!c.context) return fail(NEDO_GPU_ERR_ARG, "context_length is zero");
-    if (c.head_dim % 2u || c.head_dim > 512u) return fail(NEDO_GPU_ERR_ARG, "head_dim must be even and at most 512");
+    if (c.head_dim == 0 || c.head_dim > 1024u) return fail(NEDO_GPU_ERR_ARG, "head_dim must be in 1..1024");
     if (c.dim == 0 || c.ffn == 0 || c.vocab == 0) return fail(NEDO_GPU_ERR_ARG, "empty model dimensions");
+    if (c.dim > 25600) return fail(NEDO_GPU_ERR_ARG, "embedding_length above 25600 (RMSNorm stages it in shared memory)");
     if (n != 4u + 9ull * c.layers) return fail(NEDO_GPU_ERR_ARG, "decoder_create: expected 4 + 9 * layers tensors");
     const uint32_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
     // embedding and head
@@ -1212,8 +1271,7 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
     }
     const uint32_t sl = c.sliding ? c.sliding : c.context;
     const uint32_t window = std::max<uint32_t>(1u, std::min<uint32_t>(sl, c.context));
-    if (attention_smem_bytes(window, c.head_dim) > 200u * 1024u)
-        return fail(NEDO_GPU_ERR_ARG, "attention window too long for one CTA's shared memory");
+    if (c.head_dim % 8u) return fail(NEDO_GPU_ERR_ARG, "head_dim must be a multiple of 8");
 
     DeviceState* s = nullptr;
     if (int rc = get_state(&s)) return rc;
@@ -1224,7 +1282,8 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
     d->qd = qd;
     d->kvd = kvd;
     auto build = [&]() -> int {
-        NEDO_CUDA_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+        NEDO_CUDA_TRY(cudaStreamCreateWithFlags(&d->own_stream, cudaStreamNonBlocking));
+        d->stream = d->own_stream;
         const nedo_gpu_tensor_view* p1[1];
         p1[0] = &t[0];
         if (int rc = dec_upload(d, p1, 1, &d->emb)) return rc;
@@ -1269,6 +1328,9 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
             p1[0] = &t[b + 8];
             if (int rc = dec_upload(d, p1, 1, &L.down)) return rc;
             L.down_type = t[b + 8].type;
+            L.qkv_fused = fusable(s, L.qkv_type, qd + 2ull * kvd, c.dim);
+            L.gu_fused = fusable(s, L.gu_type, 2ull * c.ffn, c.dim);
+            L.down_fused = fusable(s, L.down_type, c.dim, c.ffn);
         }
         void* p = nullptr;
         auto vec = [&](float** f, uint64_t count) -> int {
@@ -1277,12 +1339,18 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
             return 0;
         };
         if (int rc = vec(&d->x, c.dim)) return rc;
+        if (int rc = vec(&d->x2, c.dim)) return rc;
         if (int rc = vec(&d->xn, c.dim)) return rc;
         if (int rc = vec(&d->qkv, qd + 2ull * kvd)) return rc;
         if (int rc = vec(&d->att, qd)) return rc;
         if (int rc = vec(&d->tmp, c.dim)) return rc;
         if (int rc = vec(&d->gu, 2ull * c.ffn)) return rc;
         if (int rc = vec(&d->logits, d->head_rows)) return rc;
+        if (int rc = vec(&d->attn_part, static_cast<uint64_t>(c.heads) * attention_splits(window) * (c.head_dim + 2u)))
+            return rc;
+        if (int rc = dec_alloc(d, &p, c.heads * sizeof(uint32_t))) return rc;
+        d->attn_counter = static_cast<uint32_t*>(p);
+        NEDO_CUDA_TRY(cudaMemsetAsync(d->attn_counter, 0, c.heads * sizeof(uint32_t), d->stream));
         const uint64_t cache = static_cast<uint64_t>(c.layers) * window * kvd;
         if (int rc = vec(&d->kcache, cache ? cache : 1)) return rc;
         if (int rc = vec(&d->vcache, cache ? cache : 1)) return rc;
@@ -1290,6 +1358,8 @@ int nedo_gpu_decoder_create(const nedo_gpu_decoder_config* cfg, const nedo_gpu_t
         NEDO_CUDA_TRY(cudaMemsetAsync(d->vcache, 0, (cache ? cache : 1) * sizeof(float), d->stream));
         if (int rc = dec_alloc(d, &p, sizeof(DecodeIo))) return rc;
         d->io = static_cast<DecodeIo*>(p);
+        if (int rc = dec_alloc(d, &p, static_cast<uint64_t>(c.context) * sizeof(uint32_t))) return rc;
+        d->ids = static_cast<uint32_t*>(p);
         if (int rc = dec_alloc(d, &p, 16)) return rc;
         d->amax = static_cast<int64_t*>(p);
         const size_t ncand = static_cast<size_t>(s->num_sms) + 1;
@@ -1356,6 +1426,78 @@ int nedo_gpu_decoder_forward(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, 
         }
         if (argmax_out) *argmax_out = static_cast<uint32_t>(d->pin->index);
         if (logits_host) std::memcpy(logits_host, d->logits_pin, d->head_rows * sizeof(float));
+        return 0;
+    });
+}
+
+int nedo_gpu_decoder_set_stream(nedo_gpu_decoder* d, void* stream) {
+    if (!d) return fail(NEDO_GPU_ERR_ARG, "decoder_set_stream: null decoder");
+    return on_device(d->s->device, [&]() -> int {
+        NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        for (auto& g : d->graph) {
+            if (g) cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+        if (d->gen_graph) cudaGraphExecDestroy(d->gen_graph);
+        d->gen_graph = nullptr;
+        d->eager_done[0] = d->eager_done[1] = false;
+        d->stream = stream ? static_cast<cudaStream_t>(stream) : d->own_stream;
+        return 0;
+    });
+}
+
+int nedo_gpu_decoder_generate(nedo_gpu_decoder* d, uint32_t token, uint64_t pos, uint32_t n, uint32_t* ids_host) {
+    if (!d || (n && !ids_host)) return fail(NEDO_GPU_ERR_ARG, "decoder_generate: null pointer");
+    if (token >= d->cfg.vocab || token >= d->emb_rows) return fail(NEDO_GPU_ERR_ARG, "prompt token id out of range");
+    if (n == 0) return 0;
+    if (pos + n > d->cfg.context) return fail(NEDO_GPU_ERR_ARG, "generation beyond context_length");
+    // every pick must be a valid next token: the head may have more rows than vocab
+    if (d->head_rows > d->emb_rows) return fail(NEDO_GPU_ERR_ARG, "LM head has more rows than the embedding");
+    return on_device(d->s->device, [&]() -> int {
+        if (!d->eager_done[0]) {
+            // settle kernel attributes and plans with one eager pass first
+            d->pin->io.pos = pos;
+            d->pin->io.token = token;
+            d->pin->io.step = 0;
+            if (int rc = dec_step_ops(d, false)) return rc;
+            NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+            d->eager_done[0] = true;
+        }
+        if (d->gen_graph == nullptr) {
+            cudaGraph_t g = nullptr;
+            NEDO_CUDA_TRY(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
+            int rc = dec_enqueue(d);
+            if (rc == 0) {
+                cudaError_t e = launch_advance(d->io, d->amax, d->ids, d->cfg.context, d->stream);
+                if (e != cudaSuccess) rc = cuda_fail(e, "advance launch");
+            }
+            cudaError_t e = cudaStreamEndCapture(d->stream, &g);
+            if (rc) {
+                if (g) cudaGraphDestroy(g);
+                return rc;
+            }
+            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture(decoder generate)");
+            e = cudaGraphInstantiate(&d->gen_graph, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate(decoder generate)");
+        }
+        d->pin->io.pos = pos;
+        d->pin->io.token = token;
+        d->pin->io.step = 0;
+        NEDO_CUDA_TRY(cudaMemcpyAsync(d->io, &d->pin->io, sizeof(DecodeIo), cudaMemcpyHostToDevice, d->stream));
+        for (uint32_t k = 0; k < n; ++k) NEDO_CUDA_TRY(cudaGraphLaunch(d->gen_graph, d->stream));
+        NEDO_CUDA_TRY(cudaMemcpyAsync(ids_host, d->ids, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, d->stream));
+        NEDO_CUDA_TRY(cudaMemcpyAsync(&d->pin->status, d->s->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost,
+                                      d->stream));
+        NEDO_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        if (d->pin->status.flags != 0) {
+            const DeviceStatus st = d->pin->status;
+            clear_status_flags(d->s, d->stream);
+            char buf[160];
+            std::snprintf(buf, sizeof(buf), "device kernel failed in the decode pass (flags=0x%x, site=%u)", st.flags,
+                          st.where);
+            return fail(NEDO_GPU_ERR_DEVICE, buf);
+        }
         return 0;
     });
 }

@@ -58,6 +58,8 @@ EXPORTS = (
     "nedo_gpu_plan_info",
     "nedo_gpu_decoder_create",
     "nedo_gpu_decoder_forward",
+    "nedo_gpu_decoder_generate",
+    "nedo_gpu_decoder_set_stream",
     "nedo_gpu_decoder_logits_dev",
     "nedo_gpu_decoder_reset",
     "nedo_gpu_decoder_destroy",
@@ -118,6 +120,8 @@ _SIGNATURES = {
     "nedo_gpu_decoder_create": ([ctypes.POINTER(DecoderConfig), ctypes.POINTER(TensorView), _u64, ctypes.POINTER(_vp)],
                                 _i32),
     "nedo_gpu_decoder_forward": ([_vp, _u32, _u64, _vp, ctypes.POINTER(_u32)], _i32),
+    "nedo_gpu_decoder_generate": ([_vp, _u32, _u64, _u32, _vp], _i32),
+    "nedo_gpu_decoder_set_stream": ([_vp, _vp], _i32),
     "nedo_gpu_decoder_logits_dev": ([_vp, ctypes.POINTER(_vp)], _i32),
     "nedo_gpu_decoder_reset": ([_vp], _i32),
     "nedo_gpu_decoder_destroy": ([_vp], None),

@@ -112,6 +112,17 @@ class Decoder:
                                                               ctypes.byref(idx)))
         return int(idx.value), out
 
+    def generate(self, token: int, pos: int, n: int) -> list:
+        """n greedy passes with the loop on the device (nedo_gpu_decoder_generate):
+        the picks of passes pos .. pos + n - 1, the first fed `token`."""
+        ids = np.empty(max(n, 1), np.uint32)
+        self.lib._check(self.lib.lib.nedo_gpu_decoder_generate(self.h, token, pos, n, ids.ctypes.data))
+        return [int(v) for v in ids[:n]]
+
+    def set_stream(self, stream: int) -> None:
+        """Run the passes on a caller's CUDA stream (0 = the decoder's own)."""
+        self.lib._check(self.lib.lib.nedo_gpu_decoder_set_stream(self.h, stream or None))
+
     def logits_dev(self) -> int:
         p = ctypes.c_void_p()
         self.lib._check(self.lib.lib.nedo_gpu_decoder_logits_dev(self.h, ctypes.byref(p)))

@@ -148,17 +148,15 @@ class GgufFile:
         self._f.close()
 
 
-def _weight(ttype, rows, cols, seed):
-    return B.gen_weight(ttype, rows, cols, seed).reshape(-1)
-
-
 def synthetic_model(path, dim=256, layers=2, heads=4, kv_heads=2, ffn=512, vocab=512, context=64, sliding=16,
                     wtype=Q8_0, emb_type=Q8_0, head_type=F16, norm_type=F32, tied=False, seed=1, rope_theta=10000.0,
-                    rms_eps=1e-5, morph=None):
+                    rms_eps=1e-5, morph=None, shared_layers=False):
     """A NedoLM GGUF with seeded random weights.  Projection weights as the matvec
     configurations draw them (blocks.gen_weight), norm weights
     1 + N(0, 0.1).  morph = (layers, shared, root, suffix) adds the MorphFFN
-    routing table blk.0.ffn_gate_tid2eid.weight [2, vocab] F32 of 0/1 flags."""
+    routing table blk.0.ffn_gate_tid2eid.weight [2, vocab] F32 of 0/1 flags.
+    shared_layers: every layer gets layer 0's bytes (fast to build; still one
+    tensor per layer in the file)."""
     if vocab < 259:
         raise ValueError("the surface tokenizer needs at least 259 ids")
     hd = dim // heads
@@ -195,6 +193,14 @@ def synthetic_model(path, dim=256, layers=2, heads=4, kv_heads=2, ffn=512, vocab
         v = (1.0 + 0.1 * r.standard_normal(n)).astype(np.float32)
         return (v if norm_type == F32 else v.astype(np.float16)).view(np.uint8).reshape(-1)
 
+    memo = {}
+
+    def _weight(ttype, rows, cols, sd):
+        key = (ttype, rows, cols, sd)
+        if key not in memo:
+            memo[key] = B.gen_weight(ttype, rows, cols, sd).reshape(-1)
+        return memo[key]
+
     t = []
     s = seed * 1000
     t.append(("token_embd.weight", emb_type, [dim, vocab], _weight(emb_type, vocab, dim, s + 1)))
@@ -206,7 +212,7 @@ def synthetic_model(path, dim=256, layers=2, heads=4, kv_heads=2, ffn=512, vocab
         t.append(("blk.0.ffn_gate_tid2eid.weight", F32, [2, vocab], flags.view(np.uint8).reshape(-1)))
     kvd = kv_heads * hd
     for i in range(layers):
-        b = s + 100 * (i + 1)
+        b = s + 100 * (1 if shared_layers else i + 1)
         t.append((f"blk.{i}.attn_norm.weight", norm_type, [dim], norm(dim, b)))
         t.append((f"blk.{i}.attn_q.weight", wtype, [dim, dim], _weight(wtype, dim, dim, b + 1)))
         t.append((f"blk.{i}.attn_k.weight", wtype, [dim, kvd], _weight(wtype, kvd, dim, b + 2)))

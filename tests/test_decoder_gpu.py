@@ -14,7 +14,8 @@ be the first index of its own logits' maximum, and the reference's pick
 wherever the reference's top-2 gap exceeds the tolerance.  The free-running
 greedy decode is then checked against the reference's ids, and a rerun after
 reset must give bit-identical logits (the captured graph replays the eager
-first pass)."""
+first pass).  Greedy generation with the loop on the device
+(nedo_gpu_decoder_generate) must give the reference's ids too."""
 import os
 import sys
 
@@ -74,6 +75,23 @@ def test_greedy_matches_reference_ids(model):
     assert ids == [int(i) for i in GOLDEN[name + "/ids"]]
 
 
+def test_device_generation_matches_reference_ids(model):
+    # the prompt but its last token through forward(), then the device loop from
+    # the last prompt token: pass k's pick is the reference's k-th generated id
+    name, g, dec, prompt, max_new = model
+    ref_ids = [int(i) for i in GOLDEN[name + "/ids"]]
+    dec.reset()
+    for pos, t in enumerate(prompt[:-1]):
+        dec.forward(t, pos, logits=False)
+    ids = dec.generate(prompt[-1], len(prompt) - 1, len(ref_ids))
+    assert ids == ref_ids
+    # and a second generation from the same state replays the same picks
+    dec.reset()
+    for pos, t in enumerate(prompt[:-1]):
+        dec.forward(t, pos, logits=False)
+    assert dec.generate(prompt[-1], len(prompt) - 1, len(ref_ids)) == ref_ids
+
+
 def test_rerun_is_bit_identical(model):
     name, g, dec, prompt, max_new = model
     seq = list(prompt) + [int(i) for i in GOLDEN[name + "/ids"]]
@@ -92,6 +110,9 @@ def test_decoder_argument_errors(model):
     with pytest.raises(nedo_gpu.NedoGpuError) as e:
         dec.forward(1, dec.cfg.context)
     assert e.value.code == nedo_gpu.ERR_ARG
+    with pytest.raises(nedo_gpu.NedoGpuError) as e:
+        dec.generate(1, dec.cfg.context - 2, 3)
+    assert e.value.code == nedo_gpu.ERR_ARG and "context" in str(e.value)
 
 
 def test_decoder_config_errors(cuda, tmp_path):
