@@ -151,3 +151,48 @@ def _views(g, cfg):
             v.nbytes = nb
         out.append(v)
     return out
+
+
+def _build_dropin_program():
+    import subprocess
+    import tempfile
+    exe = os.path.join(tempfile.mkdtemp(prefix="nedo_dec_"), "decoder_dropin")
+    lib_dir = os.path.join(ROOT, "nedo.cpp_b200", "lib")
+    subprocess.run(["g++", "-std=c++20", "-O2", "-I", os.path.join(ROOT, "nedo.cpp_b200", "cpp", "compat"),
+                    "-I", os.path.join(ROOT, "include"), os.path.join(ROOT, "tests", "decoder_dropin.cpp"),
+                    "-L", lib_dir, "-lnedo_kernels_cuda", "-lnedo_gpu", f"-Wl,-rpath,{lib_dir}", "-o", exe],
+                   check=True)
+    return exe
+
+
+@pytest.mark.parametrize("name", list(M.MODELS))
+def test_cpp_dropin_decoder_matches_reference(cuda, tmp_path, name):
+    """nedo::DeviceDecoder (libnedo_kernels_cuda.so), the class a NedoModel would
+    hold, over a GGUF read by a C++ reader: teacher-forced logits and the
+    device-loop generation against the reference's decode loop."""
+    import subprocess
+    kw, prompt, max_new = M.MODELS[name]
+    p = str(tmp_path / (name + ".gguf"))
+    G.synthetic_model(p, **kw)
+    ref = GOLDEN[name + "/logits"]
+    ids = [int(i) for i in GOLDEN[name + "/ids"]]
+    seq = list(prompt) + ids
+    exe = _build_dropin_program()
+    out = str(tmp_path / "out.bin")
+    r = subprocess.run([exe, p, out, str(len(ids)), str(len(prompt))] + [str(t) for t in seq[:ref.shape[0]]],
+                       capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), (r.returncode, r.stdout, r.stderr)
+    b = open(out, "rb").read()
+    a = np.frombuffer(b, dtype=np.uint32)
+    passes, vocab = int(a[0]), int(a[1])
+    lg = np.frombuffer(b, dtype=np.float32, count=passes * vocab, offset=8).reshape(passes, vocab)
+    off = 2 + passes * vocab
+    n = int(a[off])
+    picks = a[off + 1:off + 1 + passes]
+    gen = [int(v) for v in a[off + 1 + passes:off + 1 + passes + n]]
+    assert passes == ref.shape[0]
+    rel = np.abs(lg - ref).max(axis=1) / np.abs(ref).max(axis=1)
+    assert rel.max() <= LOGIT_TOL, rel
+    assert all(int(picks[k]) == int(np.argmax(lg[k])) for k in range(passes))
+    assert gen == ids
