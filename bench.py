@@ -625,15 +625,8 @@ class Ctx:
 
 
 def launches_per_call(plan, nb):
-    """Kernels of this library one matvec_dev call launches."""
-    p = plan.get("path")
-    if p == 5:  # x -> fp16, the GEMM, and the split-K fold when K is split
-        return 3 if plan.get("slots", 1) > 1 else 2
-    if p == 3 and nb > 1:  # one streaming launch per vector
-        return nb
-    if p == 4 and nb > 1:  # int8 launches of 8, 4, 2 and 1 vectors
-        return nb // 8 + bin(nb % 8).count("1")
-    return 1
+    """Kernels of this library one matvec_dev call launches (the library's own count)."""
+    return plan["launches"]
 
 
 def measure_matvec(ctx, name, steps, keep_sample=False):

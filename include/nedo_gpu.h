@@ -264,8 +264,9 @@ NEDO_GPU_API int nedo_gpu_status(void* stream);
  * matvec, 5 tcgen05 GEMM over the batch), out[1] grid,
  * out[2] threads, out[3] dynamic shared bytes, out[4] rows per tile,
  * out[5] ring slots (path 5: K splits per tile, > 1 adding a fold kernel),
- * out[6] slot bytes, out[7] warps per CTA (compute warps for path 4).
- * n = capacity of out (>= 8). */
+ * out[6] slot bytes, out[7] warps per CTA (compute warps for path 4),
+ * out[8] (when n > 8) kernels one call launches.  Path 4 with several vectors
+ * describes the first launch.  n = capacity of out (>= 8). */
 NEDO_GPU_API int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, uint32_t* out, int n);
 
 /* ---- Device-resident decode forward pass -------------------------------

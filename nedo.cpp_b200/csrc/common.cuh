@@ -119,6 +119,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     return p;
 }
 
+// L2 policy for data a few CTAs read once each (a weight tile several token groups share).
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // L2 policy for data read exactly once (the weight stream).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;

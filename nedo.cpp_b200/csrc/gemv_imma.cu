@@ -87,6 +87,7 @@ struct ImmaArgs {
     uint32_t slots;
     uint32_t unit_bytes;   // 16 * box_bytes
     uint32_t early_chunks; // slice: chunks copied before x is requested
+    uint32_t token_groups; // multi-vector slice: groups of CTAs, each computing its own vectors
     uint64_t ldx;          // floats between token vectors of x
     uint64_t ldy;          // floats between token vectors of y
     DeviceStatus* status;
@@ -665,14 +666,12 @@ __global__ void __maxnreg__(NT == 1 ? 96 : 128)
 constexpr uint32_t kSubPairs = 4;
 constexpr uint64_t kEarlyBytes = 160u * 1024u;  // weight bytes a CTA copies before requesting x
 
-// One block pair of one 16-row tile (rows g, g+8 at p0 / p1) against the x side
-// already in registers: the two IMMAs and the per-block recombination.
+// The A fragments and the two block scales of one block pair of one 16-row
+// tile (rows g, g+8 at p0 / p1).
 template <uint32_t TYPE>
-__device__ __forceinline__ void pair_tile_dot(const uint8_t* p0, const uint8_t* p1, uint32_t t, uint32_t b0lo,
-                                              uint32_t b1lo, uint32_t b0hi, uint32_t b1hi, const int4& te, float& acc0,
-                                              float& acc1) {
+__device__ __forceinline__ void load_pair_a(const uint8_t* p0, const uint8_t* p1, uint32_t t, uint32_t (&A)[2][4],
+                                            float& d0, float& d1) {
     const uint32_t scale_blk = (t >> 1) * Pair<TYPE>::kBlock;
-    uint32_t A[2][4];
     if constexpr (TYPE == kQ8_0) {
 #pragma unroll
         for (uint32_t h = 0; h < 2; ++h) {
@@ -701,8 +700,15 @@ __device__ __forceinline__ void pair_tile_dot(const uint8_t* p0, const uint8_t* 
         A[1][2] = (w2 >> 4) & m;
         A[1][3] = (w3 >> 4) & m;
     }
-    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk));
-    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk));
+    d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p0 + scale_blk));
+    d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(p1 + scale_blk));
+}
+
+// The two IMMAs of one block pair (A in registers) against one token's x side
+// and the per-block recombination into the rows' sums.
+template <uint32_t TYPE>
+__device__ __forceinline__ void pair_mma(const uint32_t (&A)[2][4], float d0, float d1, uint32_t b0lo, uint32_t b1lo,
+                                         uint32_t b0hi, uint32_t b1hi, const int4& te, float& acc0, float& acc1) {
     int d[4];
     if constexpr (TYPE == kQ8_0) {
         imma_c<false>(d, A[0][0], A[0][1], A[0][2], A[0][3], b0lo, b1lo, 0, 0, 0, 0);
@@ -716,6 +722,18 @@ __device__ __forceinline__ void pair_tile_dot(const uint8_t* p0, const uint8_t* 
     const int v1 = d[2] * 128 + d[3];
     acc0 = fmaf(dot_value<TYPE>(v0), d0 * xs, acc0);
     acc1 = fmaf(dot_value<TYPE>(v1), d1 * xs, acc1);
+}
+
+// One block pair of one 16-row tile (rows g, g+8 at p0 / p1) against the x side
+// already in registers: the two IMMAs and the per-block recombination.
+template <uint32_t TYPE>
+__device__ __forceinline__ void pair_tile_dot(const uint8_t* p0, const uint8_t* p1, uint32_t t, uint32_t b0lo,
+                                              uint32_t b1lo, uint32_t b0hi, uint32_t b1hi, const int4& te, float& acc0,
+                                              float& acc1) {
+    uint32_t A[2][4];
+    float d0, d1;
+    load_pair_a<TYPE>(p0, p1, t, A, d0, d1);
+    pair_mma<TYPE>(A, d0, d1, b0lo, b1lo, b0hi, b1hi, te, acc0, acc1);
 }
 
 // One work item: `valid` (<= kSubPairs) block pairs of nt <= R tiles whose rows
@@ -995,6 +1013,257 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
     }
 }
 
+// ---------------------------------------------------------------------------
+// Multi-vector resident slice (2 to 16 token vectors per launch, whole rows in
+// one column group).  The grid is G token groups of C CTAs: group k computes
+// the vectors [k * NT, k * NT + NT) over every tile, its C CTAs splitting the
+// tiles evenly (at most R each).  A CTA keeps its tiles resident as the
+// one-vector slice does and builds the x tables of its own NT vectors only, so
+// the table work per CTA shrinks as G grows; each weight tile is read from HBM
+// by one group and from L2 by the others.
+//
+// Compute.  Warp w takes sub-segments w, w + W, ... (kMultiSub block pairs
+// each) of all the CTA's tiles for all NT vectors: per block pair and tile the
+// A fragments are loaded once and applied to every vector's B fragments, and
+// the sums stay in registers over the warp's sub-segments.  Once every warp is
+// done, each warp's row sums go into the tables' memory (no longer read) and
+// each (tile, vector) row is added over the warps in warp order, so the result
+// depends only on the shape.
+constexpr uint32_t kMultiSub = 2;
+
+// Bytes of the tables / row-sums region of the multi-vector kernel.
+__host__ __device__ constexpr uint64_t multi_region_bytes(uint64_t nt, uint64_t pairs, uint64_t warps, uint64_t r) {
+    return nt * pairs * kPairTableBytes > warps * r * nt * 16u * 4u ? nt * pairs * kPairTableBytes
+                                                                    : warps * r * nt * 16u * 4u;
+}
+
+// One sub-segment (`valid` <= kMultiSub block pairs) of nt <= R tiles (rows g /
+// g+8 at r0 / r1 + r * tstep) for NT vectors (vector k's table at pt + k * tstride).
+template <uint32_t TYPE, uint32_t R, uint32_t NT>
+__device__ __forceinline__ void multi_dot(const uint8_t* r0, const uint8_t* r1, size_t tstep, uint32_t nt,
+                                          const uint8_t* pt, size_t tstride, uint32_t valid, uint32_t lane,
+                                          uint32_t even_mask, float (&acc0)[R][NT], float (&acc1)[R][NT]) {
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    const uint32_t t = lane & 3u;
+#pragma unroll
+    for (uint32_t p = 0; p < kMultiSub; ++p) {
+        if (p >= valid) break;
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r) {
+            if (r >= nt) break;
+            uint32_t A[2][4];
+            float d0, d1;
+            load_pair_a<TYPE>(r0 + r * tstep + p * pb, r1 + r * tstep + p * pb, t, A, d0, d1);
+#pragma unroll
+            for (uint32_t k = 0; k < NT; ++k) {
+                const uint8_t* ptk = pt + k * tstride + p * kPairTableBytes;
+                const uint2 w = *reinterpret_cast<const uint2*>(ptk + lane * 8u);
+                const int4 te = *reinterpret_cast<const int4*>(ptk + 256u + t * 16u);
+                pair_mma<TYPE>(A, d0, d1, w.x & even_mask, w.x & ~even_mask, w.y & even_mask, w.y & ~even_mask, te,
+                               acc0[r][k], acc1[r][k]);
+            }
+        }
+    }
+}
+
+// Registers: NT = 8 runs 12 consumer warps (13 warps, charged as 16) within 128,
+// fewer vectors 16 consumer warps (charged as 20) within 96.
+template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT>
+__global__ void __maxnreg__(NT >= 8 ? 128 : 96) gemv_imma_multi_kernel(const __grid_constant__ CUtensorMap map,
+                                                                      const ImmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr uint32_t pb = Pair<TYPE>::kBytes;
+    constexpr bool kQ4 = TYPE == kQ4_0;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t W = a.warps;
+    const uint32_t C = gridDim.x / a.token_groups;  // CTAs per token group
+    const uint32_t grp = blockIdx.x / C, cta = blockIdx.x - grp * C;
+    const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * cta / C);
+    const uint32_t tile_end = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * (cta + 1) / C);
+    const uint32_t my_tiles = tile_end - tile_begin;  // 1 to R (planned)
+    const uint32_t nchunk = (a.pairs_total + UP - 1u) / UP;
+    const uint32_t nunits = my_tiles * nchunk;
+    const size_t tstride = static_cast<size_t>(a.pairs_total) * kPairTableBytes;  // one vector's table
+    // [units: slots x unit_bytes, unit (t, c) at t * nchunk + c][tables: NT x tstride,
+    // later the warps' row sums][full: slots][x requested][abort flag]
+    uint8_t* table = smem + static_cast<size_t>(a.slots) * a.unit_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(table + multi_region_bytes(NT, a.pairs_total, W, R));
+    uint64_t* xbar = full + a.slots;
+    volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(xbar + 1);
+    const float* x = a.x + static_cast<size_t>(grp) * NT * a.ldx;
+    float* y = a.y + static_cast<size_t>(grp) * NT * a.ldy;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t u = 0; u < nunits; ++u) mbar_init(&full[u], 1);
+        mbar_init(xbar, W);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    __syncwarp();
+    __syncthreads();
+
+    if (warp == W) {
+        // producer (one thread), as in the one-vector slice; a tile that other
+        // token groups also read keeps the normal L2 priority
+        if (lane != 0) return;
+        const uint64_t policy = a.token_groups > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t c = 0; c < nchunk && ok; ++c) {
+            if (c == a.early_chunks) {
+                ok = mbar_wait_bounded(xbar, 0u, a.status, 24u);
+                grid_launch_dependents();
+            }
+            if (!ok) break;
+            for (uint32_t t = 0; t < my_tiles; ++t, ++issued) {
+                const uint32_t u = t * nchunk + c;
+                mbar_arrive_expect_tx(&full[u], a.unit_bytes);
+                tma_load_2d_hint(smem_addr(smem + static_cast<size_t>(u) * a.unit_bytes), &map,
+                                 static_cast<int32_t>(c * UP * pb / 8u),
+                                 static_cast<int32_t>((tile_begin + t) * kTileRows), &full[u], policy);
+            }
+        }
+        if (a.early_chunks >= nchunk) {
+            ok = mbar_wait_bounded(xbar, 0u, a.status, 24u) && ok;
+            grid_launch_dependents();
+        }
+        if (!ok) *abort_flag = 1u;
+        for (uint32_t c = 0, k = 0; c < nchunk; ++c)
+            for (uint32_t t = 0; t < my_tiles && k < issued; ++t, ++k)
+                mbar_wait_bounded(&full[t * nchunk + c], 0u, a.status, 22u);
+        return;
+    }
+
+    const uint32_t g = lane >> 2;
+    const uint32_t even_mask = g < 4 ? 0xFFFFFFFFu : 0u;
+    const size_t off_a = static_cast<size_t>(g) * a.box_bytes;
+    const size_t off_b = off_a + 8u * static_cast<size_t>(a.box_bytes);
+
+    grid_dependency_wait();  // x may come from the previous kernel
+    grid_launch_dependents();
+    {
+        // the NT vectors' tables as one table of NT * 2 * pairs blocks (vector k's
+        // blocks from k * 2 * pairs): every x load issued, the producer released,
+        // then the limbs
+        const uint32_t tid = threadIdx.x, per_pass = W * 32u / 8u, q = tid & 7u;
+        const uint32_t blocks = 2u * a.pairs_total, total = NT * blocks;  // at most per_pass * kLimbPasses (planned)
+        float4 v[kLimbPasses];
+#pragma unroll
+        for (uint32_t k = 0; k < kLimbPasses; ++k) {
+            const uint32_t f = k * per_pass + tid / 8u;
+            const uint32_t tok = f / blocks, b = f - tok * blocks;
+            v[k] = f < total ? __ldg(reinterpret_cast<const float4*>(x + tok * a.ldx + 32u * b + 4u * q))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+#pragma unroll
+        for (uint32_t k = 0; k < kLimbPasses; k += 2) {
+            // the 8 threads of a block share f (the shuffles inside span exactly them)
+            if (k * per_pass >= total) break;
+            const uint32_t f0 = k * per_pass + tid / 8u, f1 = f0 + per_pass;
+            const float4 vv[2] = {v[k], v[k + 1]};
+            const uint32_t bb[2] = {f0, f1};
+            const bool ii[2] = {f0 < total, f1 < total};
+            limb_blocks<kQ4, 2>(vv, bb, q, ii, table);
+        }
+    }
+    named_barrier_sync(1, W * 32u);
+
+    const uint32_t nsub = (a.pairs_total + kMultiSub - 1u) / kMultiSub;
+    const size_t tstep = static_cast<size_t>(nchunk) * a.unit_bytes;  // unit (t + 1, c) - unit (t, c)
+    float acc0[R][NT], acc1[R][NT];
+#pragma unroll
+    for (uint32_t r = 0; r < R; ++r)
+#pragma unroll
+        for (uint32_t k = 0; k < NT; ++k) acc0[r][k] = acc1[r][k] = 0.f;
+    bool ok = true;
+    for (uint32_t s = warp; s < nsub; s += W) {
+        const uint32_t p0 = s * kMultiSub, c = p0 / UP;  // kMultiSub divides UP: one chunk
+        if (ok && *abort_flag != 0u) ok = false;
+        for (uint32_t r = 0; r < my_tiles && ok; ++r)
+            if (!mbar_wait_bounded(&full[r * nchunk + c], 0u, a.status, 25u)) {
+                ok = false;
+                *abort_flag = 1u;
+            }
+        if (!ok) continue;
+        const uint8_t* unit = smem + static_cast<size_t>(c) * a.unit_bytes + static_cast<size_t>(p0 - c * UP) * pb;
+        const uint32_t left = a.pairs_total - p0;
+        multi_dot<TYPE, R, NT>(unit + off_a, unit + off_b, tstep, my_tiles,
+                               table + static_cast<size_t>(p0) * kPairTableBytes, tstride,
+                               left < kMultiSub ? left : kMultiSub, lane, even_mask, acc0, acc1);
+    }
+    named_barrier_sync(1, W * 32u);  // every warp is done with the tables
+    // this warp's row sums: part[warp][tile][vector][16 rows]; row r of a tile is
+    // acc0 (r < 8) or acc1 (r >= 8) of lane 4 (r mod 8) after folding the t-lanes
+    float* part = reinterpret_cast<float*>(table);
+#pragma unroll
+    for (uint32_t r = 0; r < R; ++r)
+#pragma unroll
+        for (uint32_t k = 0; k < NT; ++k) {
+            float c0 = acc0[r][k], c1 = acc1[r][k];
+            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
+            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
+            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
+            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
+            const uint32_t rr = lane & 15u;
+            const float v0 = __shfl_sync(0xFFFFFFFFu, c0, 4u * (rr & 7u));
+            const float v1 = __shfl_sync(0xFFFFFFFFu, c1, 4u * (rr & 7u));
+            if (lane < 16) part[((static_cast<size_t>(warp) * R + r) * NT + k) * 16u + lane] = rr < 8 ? v0 : v1;
+        }
+    named_barrier_sync(1, W * 32u);
+    if (*abort_flag == 0u) {
+        const uint32_t nw = nsub < W ? nsub : W;  // the warps that had sub-segments
+        const uint32_t outs = my_tiles * NT * 16u;
+        for (uint32_t i = threadIdx.x; i < outs; i += W * 32u) {
+            const uint32_t r = i / (NT * 16u), k = (i / 16u) % NT, row16 = i & 15u;
+            float sum = 0.f;
+            for (uint32_t w = 0; w < nw; ++w) sum += part[((static_cast<size_t>(w) * R + r) * NT + k) * 16u + row16];
+            const uint64_t row = static_cast<uint64_t>(tile_begin + r) * kTileRows + row16;
+            if (row < a.rows) y[k * a.ldy + row] = sum;
+        }
+    }
+}
+
+template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT>
+cudaError_t launch_multi_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                           bool pdl) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_imma_multi_kernel<TYPE, UP, R, NT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3((plan.warps + 1) * 32);
+    cfg.dynamicSmemBytes = plan.smem_bytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_imma_multi_kernel<TYPE, UP, R, NT>, map, args);
+}
+
+// Vectors per CTA: 2 (up to 8 tiles), 4 (up to 4) or 8 (up to 2): 32 row sums per lane.
+template <uint32_t TYPE>
+cudaError_t launch_multi_p(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
+                           bool pdl) {
+    constexpr uint32_t UP = TYPE == kQ4_0 ? 32u : 16u;
+    if (plan.seg_pairs != UP) return cudaErrorInvalidValue;
+    switch (plan.tokens) {
+        case 2: return launch_multi_t<TYPE, UP, 8, 2>(plan, map, args, stream, pdl);
+        case 4: return launch_multi_t<TYPE, UP, 4, 4>(plan, map, args, stream, pdl);
+        case 8: return launch_multi_t<TYPE, UP, 2, 8>(plan, map, args, stream, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 template <uint32_t TYPE, uint32_t UP, uint32_t R>
 cudaError_t launch_slice_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
                            bool pdl) {
@@ -1242,17 +1511,81 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
     return p;
 }
 
+ImmaPlan plan_imma_multi(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
+                         uint32_t tokens, uint32_t vectors_per_group) {
+    ImmaPlan p;
+    if (type != kQ8_0 && type != kQ4_0) return p;
+    if (tokens < 2 || cols % 64u || cols > 0xFFFFFFFFull || rows == 0 || rows >= 0x80000000ull || num_sms <= 0)
+        return p;
+    const uint64_t rb = row_bytes_of(type, cols);
+    if (rb % 16u) return p;  // the tensor map's row stride
+    const uint64_t pair_bytes = type == kQ8_0 ? 68u : 36u;
+    const uint64_t pairs_total = cols / 64u;
+    // units of 16 rows x 32 (Q4_0) or 16 (Q8_0) block pairs, as the one-vector slice
+    const uint64_t up = type == kQ4_0 ? 32u : 16u;
+    if (up / 2u >= pairs_total) return p;
+    const uint64_t box = box_row_bytes(up, pair_bytes);
+    const uint64_t unit = kTileRows * box;
+    const uint64_t nchunk = (pairs_total + up - 1) / up;
+    const uint64_t tiles = (rows + kTileRows - 1) / kTileRows;
+    const uint32_t per_group[3] = {2u, 4u, 8u};
+    for (uint32_t nt : per_group) {
+        if (vectors_per_group && nt != vectors_per_group) continue;
+        if (tokens % nt) continue;
+        const uint64_t groups = tokens / nt;
+        const uint64_t r_max = 16u / nt;  // tiles per CTA (the kernel's R)
+        uint64_t ctas = static_cast<uint64_t>(num_sms) / groups;
+        if (ctas == 0) continue;
+        if (ctas > tiles) ctas = tiles;
+        const uint64_t tpc = (tiles + ctas - 1) / ctas;
+        if (tpc > r_max) continue;
+        const uint64_t warps = nt >= 8 ? 12u : kMaxWarps;
+        // every (vector, block) of the tables in one pass of the consumer threads' registers
+        if (nt * 2u * pairs_total > warps * 4u * kLimbPasses) continue;
+        const uint64_t slots = tpc * nchunk;
+        const uint64_t smem = slots * unit + multi_region_bytes(nt, pairs_total, warps, r_max) + 8u * slots + 16u;
+        if (smem > static_cast<uint64_t>(max_smem_optin)) continue;
+        p.type = type;
+        p.wide = true;
+        p.slice = false;
+        p.multi = true;
+        p.warps = static_cast<uint32_t>(warps);
+        p.team = 1;
+        p.tokens = nt;
+        p.token_groups = static_cast<uint32_t>(groups);
+        p.seg_pairs = static_cast<uint32_t>(up);
+        p.tile_rows = kTileRows;
+        p.tiles = static_cast<uint32_t>(tiles);
+        p.slots = static_cast<uint32_t>(slots);
+        p.unit_bytes = static_cast<uint32_t>(unit);
+        p.box_bytes = static_cast<uint32_t>(box);
+        p.grid = static_cast<uint32_t>(groups * ctas);
+        p.smem_bytes = static_cast<uint32_t>(smem);
+        p.groups = 1;
+        p.group_pairs = static_cast<uint32_t>(pairs_total);
+        p.tile_group = static_cast<uint32_t>(r_max);
+        const uint64_t chunk_bytes = tpc * unit;
+        uint64_t early = kEarlyBytes / chunk_bytes;
+        if (early < 1) early = 1;
+        p.early_chunks = static_cast<uint32_t>(early < nchunk ? early : nchunk);
+        p.ok = true;
+        return p;
+    }
+    return p;
+}
+
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather, uint64_t ldx,
                         uint64_t ldy, const XPrologue* prologue) {
     if (prologue && prologue->mode != kPrologueNone && !plan.slice) return cudaErrorInvalidValue;
+    if (plan.multi && (plan.token_groups == 0 || plan.grid % plan.token_groups != 0)) return cudaErrorInvalidValue;
     if (!plan.ok || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
         return cudaErrorInvalidValue;
     if (ldx == 0) ldx = cols;
     if (ldy == 0) ldy = rows;
     // x rows are read as float4: every token vector starts on a 16-byte boundary
-    if (plan.tokens > 1 && (ldx % 4u != 0 || ldx < cols || ldy < rows)) return cudaErrorInvalidValue;
-    if (gather != nullptr && plan.tokens != 1) return cudaErrorInvalidValue;
+    if ((plan.tokens > 1 || plan.multi) && (ldx % 4u != 0 || ldx < cols || ldy < rows)) return cudaErrorInvalidValue;
+    if (gather != nullptr && (plan.tokens != 1 || plan.multi)) return cudaErrorInvalidValue;
     ImmaArgs a{};
     if (gather != nullptr) {
         if (gather->npeers > kMaxPeers) return cudaErrorInvalidValue;
@@ -1290,7 +1623,12 @@ cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, flo
     a.ldy = ldy;
     a.status = status;
     a.early_chunks = plan.early_chunks;
+    a.token_groups = plan.token_groups;
     if (prologue) a.pro = *prologue;
+    if (plan.multi) {
+        if (plan.type == kQ8_0) return launch_multi_p<kQ8_0>(plan, map, a, stream, pdl);
+        return launch_multi_p<kQ4_0>(plan, map, a, stream, pdl);
+    }
     if (plan.slice) {
         if (plan.type == kQ8_0) return launch_slice_p<kQ8_0>(plan, map, a, stream, pdl);
         return launch_slice_p<kQ4_0>(plan, map, a, stream, pdl);

@@ -63,6 +63,8 @@ struct ImmaPlan {
     bool slice = false;        // resident slice: every unit of a CTA in its own slot (gemv_imma_slice_kernel)
     uint32_t tile_group = 0;   // slice: tiles sharing one read of the x side
     uint32_t early_chunks = 0; // slice: column chunks copied before x is requested
+    bool multi = false;        // multi-vector resident slice (gemv_imma_multi_kernel)
+    uint32_t token_groups = 0; // multi: groups of CTAs, `tokens` vectors each
     uint32_t type = 0;
     uint32_t warps = 0;        // consumer warps; one more warp streams units
     uint32_t team = 0;         // warps sharing one tile (its segments split among them)
@@ -91,6 +93,12 @@ struct ImmaTuning {
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
                    const ImmaTuning* tune = nullptr, uint32_t tokens = 1);
+
+// The multi-vector resident slice for exactly `tokens` (>= 2) vectors in one
+// launch: token groups of 2, 4 or 8 vectors (the most groups that fit; only
+// `vectors_per_group` when it is non-zero), or !ok when none fits.
+ImmaPlan plan_imma_multi(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
+                         uint32_t tokens, uint32_t vectors_per_group = 0);
 
 // Fused all-gather of a row-sharded matvec over NVLink: the kernel also stores
 // its rows into every peer's gathered y and counts each finished CTA on the

@@ -344,6 +344,52 @@ bool tc8_enabled() {
     return on;
 }
 
+// Most token vectors one multi-vector launch takes.
+constexpr uint32_t kMultiMaxVectors = 16;
+
+// NEDO_GPU_IMMA_MULTI: "0" keeps small batches on the ring kernel (for
+// comparisons), "2" / "4" / "8" fixes the vectors per token group (-1, 0 or
+// that number).
+int multi_vectors_per_group() {
+    static const int v = [] {
+        const char* e = std::getenv("NEDO_GPU_IMMA_MULTI");
+        if (e == nullptr || e[0] == '\0') return 0;
+        if (std::strcmp(e, "0") == 0) return -1;
+        const int n = std::atoi(e);
+        return n == 2 || n == 4 || n == 8 ? n : 0;
+    }();
+    return v;
+}
+
+// Small batches of Q8_0 / Q4_0 rows run on the multi-vector resident slice
+// when it plans 2 vectors (or the fixed group size).
+bool multi_applies(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols) {
+    if ((type != kQ8_0 && type != kQ4_0) || multi_vectors_per_group() < 0) return false;
+    const uint32_t g = multi_vectors_per_group();
+    return plan_imma_multi(type, rows, cols, s->num_sms, s->max_smem, g > 0 ? g : 2u, g).ok;
+}
+
+// The launches of a batch on the multi-vector slice, in order: launches of up
+// to kMultiMaxVectors vectors (the most that plan), each(&plan, first, n), and
+// single vectors (each(nullptr, first, 1)) for the rest.
+template <typename F>
+void for_each_multi_launch(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch, F&& each) {
+    for (uint32_t b = 0; b < batch;) {
+        const uint32_t left = batch - b;
+        ImmaPlan mp;
+        for (uint32_t n = left < kMultiMaxVectors ? left : kMultiMaxVectors; n >= 2 && !mp.ok; --n)
+            mp = plan_imma_multi(type, rows, cols, s->num_sms, s->max_smem, n, multi_vectors_per_group());
+        if (!mp.ok) {
+            // one vector left, or none of the fixed group size
+            for (uint32_t k = 0; k < left; ++k) each(static_cast<const ImmaPlan*>(nullptr), b + k, 1u);
+            return;
+        }
+        const uint32_t n = mp.tokens * mp.token_groups;
+        each(static_cast<const ImmaPlan*>(&mp), b, n);
+        b += n;
+    }
+}
+
 // The one dispatch point for every matvec launch.
 int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, const void* w, const float* x,
                     float* y, uint32_t batch, const ArgmaxScratch* amax, cudaStream_t stream, int pdl_override = -1) {
@@ -399,6 +445,23 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
         e = launch_gemm_tc(type, w, s->xh, y, rows, cols, batch, rows, s->status, stream, use_pdl);
         if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
         return 0;
+    }
+    if (batch > 1 && amax == nullptr && aligned16(w) && aligned16(x) && multi_applies(s, type, rows, cols)) {
+        // small batches of quantised rows on the multi-vector resident slice
+        int rc = 0;
+        for_each_multi_launch(s, type, rows, cols, batch, [&](const ImmaPlan* mp, uint32_t b, uint32_t n) {
+            const float* xb = x + static_cast<uint64_t>(b) * cols;
+            float* yb = y + static_cast<uint64_t>(b) * rows;
+            if (rc) return;
+            if (mp == nullptr) {
+                rc = dispatch_matvec(s, type, rows, cols, w, xb, yb, 1, nullptr, stream, pdl_override);
+                return;
+            }
+            cudaError_t e = launch_imma(*mp, w, xb, yb, rows, cols, s->status, stream, use_pdl, nullptr, cols, rows);
+            if (e != cudaSuccess) rc = cuda_fail(e, "gemv_imma multi-vector launch");
+            (void)n;
+        });
+        return rc;
     }
     if (batch > 1 && amax == nullptr && aligned16(w) && aligned16(x) && (type == kQ8_0 || type == kQ4_0)) {
         // small batches of quantised rows: the int8 tensor-pipe kernel with up to 8
@@ -928,12 +991,25 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             out[5] = tp.slots;
             out[6] = tp.unit_bytes;
             out[7] = 8;  // loader + epilogue warps
+            if (n > 8) out[8] = 1;
             return 0;
         }
     }
-    if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches of up to 8 vectors
+    if (!tc && (type == kQ8_0 || type == kQ4_0)) {  // int8 tensor-pipe launches
         const uint32_t tokens = batch >= 8 ? 8u : batch >= 4 ? 4u : batch >= 2 ? 2u : 1u;
         ImmaPlan ip = plan_imma(type, rows, cols, s->num_sms, s->max_smem, nullptr, tokens);
+        // ring kernel: launches of 8, 4, 2 and 1 vectors
+        uint32_t launches = batch <= 1 ? 1u : batch / 8u + static_cast<uint32_t>(__builtin_popcount(batch % 8u));
+        if (batch >= 2 && multi_applies(s, type, rows, cols)) {
+            // the first multi-vector launch, and the launch count, as dispatch_matvec plans them
+            bool first = true;
+            launches = 0;
+            for_each_multi_launch(s, type, rows, cols, batch, [&](const ImmaPlan* mp, uint32_t, uint32_t) {
+                ++launches;
+                if (first && mp != nullptr) ip = *mp;
+                first = false;
+            });
+        }
         if (ip.ok) {
             out[0] = 4;
             out[1] = ip.grid;
@@ -943,6 +1019,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             out[5] = ip.slots;
             out[6] = ip.unit_bytes;
             out[7] = ip.warps;
+            if (n > 8) out[8] = launches;
             return 0;
         }
     }
@@ -957,6 +1034,7 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
             out[5] = p.slots;
             out[6] = p.slot_bytes;
             out[7] = p.warps;
+            if (n > 8) out[8] = 1;
             return 0;
         }
     }
@@ -966,9 +1044,11 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
         out[2] = 320;
         out[4] = 128;
         out[5] = gemm_tc_splits(rows, cols, batch, s->num_sms);  // K splits (> 1: a fold kernel follows)
+        if (n > 8) out[8] = out[5] > 1 ? 3u : 2u;  // x to fp16, the GEMM (, the fold)
         return 0;
     }
     out[0] = batch > 1 ? 3 : 2;
+    if (n > 8) out[8] = batch > 1 && out[0] == 3 ? batch : 1u;
     return 0;
 }
 

@@ -274,9 +274,9 @@ class Library:
         self._check(self.lib.nedo_gpu_status(stream))
 
     def plan_info(self, type_, rows, cols, batch=1) -> dict:
-        out = (_u32 * 8)()
-        self._check(self.lib.nedo_gpu_plan_info(type_, rows, cols, batch, out, 8))
-        keys = ("path", "grid", "threads", "smem_bytes", "rows_per_tile", "slots", "slot_bytes", "warps")
+        out = (_u32 * 9)()
+        self._check(self.lib.nedo_gpu_plan_info(type_, rows, cols, batch, out, 9))
+        keys = ("path", "grid", "threads", "smem_bytes", "rows_per_tile", "slots", "slot_bytes", "warps", "launches")
         return dict(zip(keys, list(out)))
 
 
