@@ -10,6 +10,8 @@
 // with griddepcontrol.wait (programmatic dependent launch) before it reads
 // anything that predecessor wrote.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "launch.h"
@@ -114,191 +116,398 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 // (src/kernels.cpp:93-105) and the KV-cache write included, split over keys.
 // CTA (s, h) takes keys [s * kKeys, (s + 1) * kKeys) of the window of query
 // head h:
+//   * before the dependency wait, the split's cached keys and values are
+//     copied into shared memory (cp.async, L2 only): the cache was written by
+//     earlier passes, which completed before the previous kernel of this pass
+//     passed its own dependency wait, and the position comes from `io`, which
+//     the previous pass's last kernel (or the host) wrote;
 //   * RoPE of q_h (every CTA of the head computes the same rotated vector);
 //   * the current position's key and value (the last key of the window) are
-//     rotated / copied from qkv by the CTAs whose split holds that key and used
-//     from shared memory; the first query head of each KV group also writes
-//     them into cache slot pos % window (no CTA of this pass reads that slot
-//     from the cache: its previous occupant is outside the window);
-//   * scores q.k / sqrt(hd) with the dot in double (two threads per key, half
-//     the dimensions each), the split's maximum m_s, e_j = exp(score_j - m_s),
-//     l_s = sum e_j and acc_s[d] = sum_j e_j v_j[d] (keys in order);
-//   * the last CTA of the head to finish (a self-resetting counter) adds the
-//     splits in split order: out[d] = sum_s acc_s[d] w_s / sum_s l_s w_s with
-//     w_s = exp(m_s - M), M = max_s m_s -- the same result whichever CTA is last.
-constexpr uint32_t kKeys = 64;
+//     rotated / copied from qkv by the CTA whose split holds that key; the
+//     first query head of each KV group also writes them into cache slot
+//     pos % window (no CTA of this pass reads that slot from the cache: its
+//     previous occupant is outside the window);
+//   * scores q.k / sqrt(hd) with the dot in double (lane = key, the warps a
+//     quarter of the dimensions each, added in warp order), the split's
+//     maximum m_s, e_j = exp(score_j - m_s), l_s = sum e_j and
+//     acc_s[d] = sum_j e_j v_j[d] (keys in order);
+//   * the last of the head's non-empty splits to finish (a self-resetting
+//     counter) adds them in split order, out[d] = sum_s acc_s[d] w_s /
+//     sum_s l_s w_s with w_s = exp(m_s - M), M the running maximum over rounds
+//     of 16 splits -- the same result whichever CTA is last.  Splits past the
+//     window's keys do nothing.
+constexpr uint32_t kKeys = 32;  // keys per split: one per lane
 constexpr uint32_t kAttnWarps = 4;
 constexpr uint32_t kAttnThreads = 32 * kAttnWarps;
-constexpr uint32_t kKeysPerWarp = kKeys / kAttnWarps;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// Threads per value dimension: the largest power of two <= kAttnThreads / hd (>= 1).
+__host__ __device__ constexpr uint32_t value_parts(uint32_t hd) {
+    uint32_t p = 1;
+    while (2u * p * hd <= kAttnThreads) p *= 2u;
+    return p;
+}
+
+// Shared floats of attention_kernel: keys and values [kKeys][hd + 4], q [hd],
+// the value partials [max(kAttnThreads, hd)].
+__host__ __device__ constexpr size_t attention_smem_floats(uint32_t hd) {
+    return 2u * kKeys * static_cast<size_t>(hd + 4u) + static_cast<size_t>(hd) +
+           (hd > kAttnThreads ? hd : kAttnThreads);
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const float* __restrict__ qkv, float* __restrict__ kcache, float* __restrict__ vcache, float* __restrict__ part,
     float* __restrict__ att, uint32_t* __restrict__ counter, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
     uint32_t window, float theta, float inv_sqrt_hd) {
-    // q rotated [hd], current k [hd], current v [hd], value sums [warps][hd], split weights [nsplit]
     extern __shared__ __align__(16) float sm[];
-    __shared__ float sc[kKeys];
-    __shared__ float red[kAttnWarps];
+    __shared__ double dpart[kAttnWarps][kKeys];
+    __shared__ float ew[kKeys];
+    __shared__ float ml[2];
     __shared__ uint32_t last;
-    dep_wait();
-    dep_launch();
-    const uint64_t pos = io->pos;
+    const uint32_t pitch = hd + 4u;  // an odd number of float4s: lane-per-row reads hit distinct banks
+    float* ks = sm;
+    float* vs = ks + kKeys * pitch;
+    float* qs = vs + kKeys * pitch;
+    float* vp = qs + hd;
+    const uint64_t pos = __ldcg(reinterpret_cast<const unsigned long long*>(&io->pos));
     const uint32_t s = blockIdx.x, h = blockIdx.y, qpk = nq / nkv, kh = h / qpk, kvd = nkv * hd;
-    const uint32_t nsplit = gridDim.x, t = threadIdx.x, half = hd / 2u;
+    const uint32_t t = threadIdx.x, half = hd / 2u;
     const uint32_t warp = t >> 5, lane = t & 31u, hd4 = hd / 4u;
-    float* qs = sm;
-    float* kcur = sm + hd;
-    float* vcur = sm + 2u * hd;
-    float* pv = sm + 3u * hd;
-    float* wsp = sm + (3u + kAttnWarps) * hd;
     const uint64_t start = pos + 1 > window ? pos + 1 - window : 0;
     const uint32_t nctx = static_cast<uint32_t>(pos - start + 1);
+    const uint32_t nused = (nctx + kKeys - 1u) / kKeys;  // splits holding keys
     const uint32_t j0 = s * kKeys;
-    const uint32_t nk = nctx > j0 ? (nctx - j0 < kKeys ? nctx - j0 : kKeys) : 0u;
+    if (s >= nused) return;  // reads and writes nothing
+    const uint32_t nk = nctx - j0 < kKeys ? nctx - j0 : kKeys;
     const uint32_t jcur = nctx - 1;  // the current position's key
-    const bool has_cur = nk > 0 && jcur >= j0 && jcur < j0 + nk;
+    const bool has_cur = jcur >= j0 && jcur < j0 + nk;
     const size_t cur_slot = static_cast<size_t>(pos % window) * kvd + static_cast<size_t>(kh) * hd;
-    float* out = part + (static_cast<size_t>(h) * nsplit + s) * (hd + 2u);
-    if (nk > 0) {
-        const float* q = qkv + static_cast<size_t>(h) * hd;
-        const float* k = qkv + static_cast<size_t>(nq) * hd + static_cast<size_t>(kh) * hd;
-        const float* v = qkv + static_cast<size_t>(nq) * hd + kvd + static_cast<size_t>(kh) * hd;
-        for (uint32_t i = t; i < half; i += kAttnThreads) {
-            const float freq = powf(theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
-            const float a = static_cast<float>(pos) * freq;
-            const float c = cosf(a), sn = sinf(a);
-            const float x0 = q[i], y0 = q[i + half];
-            qs[i] = x0 * c - y0 * sn;
-            qs[i + half] = x0 * sn + y0 * c;
-            if (has_cur) {
-                const float kx = k[i], ky = k[i + half];
-                kcur[i] = kx * c - ky * sn;
-                kcur[i + half] = kx * sn + ky * c;
-                vcur[i] = v[i];
-                vcur[i + half] = v[i + half];
+    for (uint32_t i = t; i < nk * hd4; i += kAttnThreads) {
+        const uint32_t j = i / hd4, c = i - j * hd4;
+        if (j0 + j == jcur) continue;
+        const size_t off = static_cast<size_t>((start + j0 + j) % window) * kvd + static_cast<size_t>(kh) * hd + 4u * c;
+        cp_async16(ks + j * pitch + 4u * c, kcache + off);
+        cp_async16(vs + j * pitch + 4u * c, vcache + off);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    dep_wait();
+    dep_launch();
+    const float* q = qkv + static_cast<size_t>(h) * hd;
+    const float* k = qkv + static_cast<size_t>(nq) * hd + static_cast<size_t>(kh) * hd;
+    const float* v = qkv + static_cast<size_t>(nq) * hd + kvd + static_cast<size_t>(kh) * hd;
+    for (uint32_t i = t; i < half; i += kAttnThreads) {
+        const float freq = powf(theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+        const float a = static_cast<float>(pos) * freq;
+        const float c = cosf(a), sn = sinf(a);
+        const float x0 = q[i], y0 = q[i + half];
+        qs[i] = x0 * c - y0 * sn;
+        qs[i + half] = x0 * sn + y0 * c;
+        if (has_cur) {
+            const float kx = k[i], ky = k[i + half];
+            const float k0 = kx * c - ky * sn, k1 = kx * sn + ky * c;
+            const float v0 = v[i], v1 = v[i + half];
+            float* kr = ks + (jcur - j0) * pitch;
+            float* vr = vs + (jcur - j0) * pitch;
+            kr[i] = k0;
+            kr[i + half] = k1;
+            vr[i] = v0;
+            vr[i + half] = v1;
+            if (h % qpk == 0) {
+                kcache[cur_slot + i] = k0;
+                kcache[cur_slot + i + half] = k1;
+                vcache[cur_slot + i] = v0;
+                vcache[cur_slot + i + half] = v1;
             }
         }
-        __syncthreads();
-        if (has_cur && h % qpk == 0) {
-            for (uint32_t d = t; d < hd; d += kAttnThreads) {
-                kcache[cur_slot + d] = kcur[d];
-                vcache[cur_slot + d] = vcur[d];
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // scores: lane = key, warp w the dimension chunks w, w + 4, ...
+    {
+        double acc = 0.0;
+        if (lane < nk) {
+            const float4* kr = reinterpret_cast<const float4*>(ks + lane * pitch);
+            const float4* q4p = reinterpret_cast<const float4*>(qs);
+            for (uint32_t c = warp; c < hd4; c += kAttnWarps) {
+                const float4 q4 = q4p[c], k4 = kr[c];
+                acc += static_cast<double>(q4.x) * k4.x;
+                acc += static_cast<double>(q4.y) * k4.y;
+                acc += static_cast<double>(q4.z) * k4.z;
+                acc += static_cast<double>(q4.w) * k4.w;
             }
         }
-        // scores: warp w takes keys w * kKeysPerWarp .. + kKeysPerWarp, the lanes a
-        // key's dimensions as float4s (coalesced rows, all the warp's keys in flight)
-        const float* krow[kKeysPerWarp];
-#pragma unroll
-        for (uint32_t i = 0; i < kKeysPerWarp; ++i) {
-            const uint32_t j = warp * kKeysPerWarp + i;
-            const uint32_t slot = static_cast<uint32_t>((start + j0 + j) % window);
-            krow[i] = (j0 + j == jcur) ? kcur : kcache + static_cast<size_t>(slot) * kvd + static_cast<size_t>(kh) * hd;
+        dpart[warp][lane] = acc;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        double d = dpart[0][lane];
+        for (uint32_t w = 1; w < kAttnWarps; ++w) d += dpart[w][lane];
+        const float sc = lane < nk ? static_cast<float>(d) * inv_sqrt_hd : -INFINITY;
+        float m = sc;
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        const float e = lane < nk ? expf(sc - m) : 0.f;
+        float l = e;
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+        ew[lane] = e;
+        if (lane == 0) {
+            ml[0] = m;
+            ml[1] = l;
         }
-        double pacc[kKeysPerWarp];
-#pragma unroll
-        for (uint32_t i = 0; i < kKeysPerWarp; ++i) pacc[i] = 0.0;
-        for (uint32_t d4 = lane; d4 < hd4; d4 += 32u) {
-            const float4 q4 = reinterpret_cast<const float4*>(qs)[d4];
-            float4 kk[kKeysPerWarp];
-#pragma unroll
-            for (uint32_t i = 0; i < kKeysPerWarp; ++i)
-                kk[i] = warp * kKeysPerWarp + i < nk ? reinterpret_cast<const float4*>(krow[i])[d4]
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (uint32_t i = 0; i < kKeysPerWarp; ++i) {
-                pacc[i] += static_cast<double>(q4.x) * kk[i].x;
-                pacc[i] += static_cast<double>(q4.y) * kk[i].y;
-                pacc[i] += static_cast<double>(q4.z) * kk[i].z;
-                pacc[i] += static_cast<double>(q4.w) * kk[i].w;
-            }
-        }
-#pragma unroll
-        for (uint32_t i = 0; i < kKeysPerWarp; ++i) {
-            double dsum = pacc[i];
-            for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xFFFFFFFFu, dsum, o);
-            const uint32_t j = warp * kKeysPerWarp + i;
-            if (lane == 0) sc[j] = j < nk ? static_cast<float>(dsum) * inv_sqrt_hd : -INFINITY;
-        }
-        __syncthreads();
-        float m = t < kKeys ? sc[t] : -INFINITY;
-        m = block_max(m, red);
-        const float e = (t < kKeys && t < nk) ? expf(sc[t] - m) : 0.f;
-        __syncthreads();
-        if (t < kKeys) sc[t] = e;
-        const float l = block_sum(e, red);
-        __syncthreads();
-        // values: the same split of keys over warps, float4s over the lanes
-        for (uint32_t d4 = lane; d4 < hd4; d4 += 32u) {
-            float4 vv[kKeysPerWarp];
-#pragma unroll
-            for (uint32_t i = 0; i < kKeysPerWarp; ++i) {
-                const uint32_t j = warp * kKeysPerWarp + i;
-                const uint32_t slot = static_cast<uint32_t>((start + j0 + j) % window);
-                const float* vr = (j0 + j == jcur) ? vcur
-                                                   : vcache + static_cast<size_t>(slot) * kvd + static_cast<size_t>(kh) * hd;
-                vv[i] = j < nk ? reinterpret_cast<const float4*>(vr)[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (uint32_t i = 0; i < kKeysPerWarp; ++i) {
-                const float ej = sc[warp * kKeysPerWarp + i];
-                acc.x = fmaf(ej, vv[i].x, acc.x);
-                acc.y = fmaf(ej, vv[i].y, acc.y);
-                acc.z = fmaf(ej, vv[i].z, acc.z);
-                acc.w = fmaf(ej, vv[i].w, acc.w);
-            }
-            reinterpret_cast<float4*>(pv + warp * hd)[d4] = acc;
+    }
+    __syncthreads();
+    // values: P threads per dimension, each a contiguous run of kKeys / P keys
+    float* out = part + (static_cast<size_t>(h) * gridDim.x + s) * (hd + 2u);
+    {
+        const uint32_t P = value_parts(hd), run = kKeys / P;
+        for (uint32_t i = t; i < hd * P; i += kAttnThreads) {
+            const uint32_t d = i % hd, p = i / hd;
+            float acc = 0.f;
+            for (uint32_t j = p * run; j < p * run + run && j < nk; ++j) acc = fmaf(ew[j], vs[j * pitch + d], acc);
+            vp[p * hd + d] = acc;
         }
         __syncthreads();
         for (uint32_t d = t; d < hd; d += kAttnThreads) {
-            float acc = pv[d];
-            for (uint32_t w = 1; w < kAttnWarps; ++w) acc += pv[w * hd + d];
+            float acc = vp[d];
+            for (uint32_t p = 1; p < P; ++p) acc += vp[p * hd + d];
             out[d] = acc;
         }
         if (t == 0) {
-            out[hd] = m;
-            out[hd + 1] = l;
-        }
-    } else {
-        // no keys in this split: m = -inf, l = 0
-        for (uint32_t d = t; d < hd; d += kAttnThreads) out[d] = 0.f;
-        if (t == 0) {
-            out[hd] = -INFINITY;
-            out[hd + 1] = 0.f;
+            out[hd] = ml[0];
+            out[hd + 1] = ml[1];
         }
     }
-    // the last CTA of the head combines the splits
+    // the last non-empty split of the head combines them
     __threadfence();
     __syncthreads();
-    if (t == 0) last = atomicAdd(&counter[h], 1u) == nsplit - 1u ? 1u : 0u;
+    if (t == 0) last = atomicAdd(&counter[h], 1u) == nused - 1u ? 1u : 0u;
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // every split's (m, l) in one round of loads, the weights w_s = exp(m_s - M)
-    // in shared memory, then the value sums (loads of all splits in flight)
-    const float* p = part + static_cast<size_t>(h) * nsplit * (hd + 2u);
-    float mloc = -INFINITY;
-    for (uint32_t i = t; i < nsplit; i += kAttnThreads) {
-        const float mi = __ldcg(p + static_cast<size_t>(i) * (hd + 2u) + hd);
-        wsp[i] = mi;
-        mloc = fmaxf(mloc, mi);
-    }
-    const float mx = block_max(mloc, red);
-    float lloc = 0.f;
-    for (uint32_t i = t; i < nsplit; i += kAttnThreads) {
-        const float wi = expf(wsp[i] - mx);
-        wsp[i] = wi;
-        lloc += __ldcg(p + static_cast<size_t>(i) * (hd + 2u) + hd + 1u) * wi;
-    }
-    const float L = block_sum(lloc, red);
-    __syncthreads();
-    const float inv = 1.0f / L;
+    // each thread's dimension: the splits' (m, l) and value sums, 16 splits per
+    // round of loads, folded in split order with a running maximum (the same
+    // maxima in every thread)
+    const float* p = part + static_cast<size_t>(h) * gridDim.x * (hd + 2u);
     for (uint32_t d = t; d < hd; d += kAttnThreads) {
-        float acc = 0.f;
-#pragma unroll 8
-        for (uint32_t i = 0; i < nsplit; ++i) acc = fmaf(__ldcg(p + static_cast<size_t>(i) * (hd + 2u) + d), wsp[i], acc);
-        att[static_cast<size_t>(h) * hd + d] = acc * inv;
+        float M = -INFINITY, L = 0.f, O = 0.f;
+        for (uint32_t i0 = 0; i0 < nused; i0 += 16u) {
+            const uint32_t nb = nused - i0 < 16u ? nused - i0 : 16u;
+            float mi[16], li[16], ai[16];
+#pragma unroll
+            for (uint32_t k2 = 0; k2 < 16; ++k2) {
+                if (k2 < nb) {
+                    const float* pk = p + static_cast<size_t>(i0 + k2) * (hd + 2u);
+                    mi[k2] = __ldcg(pk + hd);
+                    li[k2] = __ldcg(pk + hd + 1u);
+                    ai[k2] = __ldcg(pk + d);
+                }
+            }
+            float mb = M;
+#pragma unroll
+            for (uint32_t k2 = 0; k2 < 16; ++k2)
+                if (k2 < nb) mb = fmaxf(mb, mi[k2]);
+            const float sc = expf(M - mb);  // 0 on the first round
+            L *= sc;
+            O *= sc;
+#pragma unroll
+            for (uint32_t k2 = 0; k2 < 16; ++k2) {
+                if (k2 < nb) {
+                    const float w = expf(mi[k2] - mb);
+                    L = fmaf(li[k2], w, L);
+                    O = fmaf(ai[k2], w, O);
+                }
+            }
+            M = mb;
+        }
+        att[static_cast<size_t>(h) * hd + d] = O / L;
     }
     if (t == 0) counter[h] = 0u;
+}
+
+// Attention as one cluster of kClusterCtas CTAs per query head, for windows
+// whose keys per CTA fit in shared memory.  CTA r of head h takes the keys
+// [r * per, (r + 1) * per) of the window, per = ceil(n / kClusterCtas); its
+// cached keys and values are copied into shared memory before the dependency
+// wait and the current position's key and value come from qkv, as in
+// attention_kernel.  Warp w runs an online softmax over the CTA's 32-key
+// chunks w, w + 4, ...: per chunk the scores (lane = key, the dot in double),
+// the running maximum m, the sum l and the value sums acc[d] (lanes =
+// dimensions), rescaled by exp(m_old - m).  Every warp's (acc, m, l) goes
+// into the cluster leader's shared memory (distributed shared-memory
+// stores); after one cluster barrier the leader adds the partials in (CTA,
+// warp) order -- out[d] = sum_i acc_i[d] w_i / sum_i l_i w_i, w_i = exp(m_i - M)
+// -- and writes the head's output: no global round trip, no counter.
+constexpr uint32_t kClusterCtas = 8;
+constexpr uint32_t kMaxClusterHd = 256;
+constexpr uint32_t kClusterParts = kClusterCtas * kAttnWarps;
+
+// Keys one CTA of the cluster kernel holds: ceil(window / kClusterCtas) rounded up to 32.
+__host__ __device__ constexpr uint32_t cluster_keys_cap(uint32_t window) {
+    return ((window + kClusterCtas - 1u) / kClusterCtas + 31u) / 32u * 32u;
+}
+
+// Shared floats of attention_cluster_kernel: keys and values [cap][hd + 4], q [hd],
+// the partial slots [kClusterParts][hd + 2].
+__host__ __device__ constexpr size_t attention_cluster_smem_floats(uint32_t hd, uint32_t window) {
+    return 2u * static_cast<size_t>(cluster_keys_cap(window)) * (hd + 4u) + hd +
+           static_cast<size_t>(kClusterParts) * (hd + 2u);
+}
+
+__device__ __forceinline__ uint32_t cluster_cta_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr(p)), "r"(rank));
+    return d;
+}
+
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kAttnThreads)
+    attention_cluster_kernel(const float* __restrict__ qkv, float* __restrict__ kcache, float* __restrict__ vcache,
+                             float* __restrict__ att, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
+                             uint32_t window, float theta, float inv_sqrt_hd) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float wsl[kClusterParts];
+    const uint32_t pitch = hd + 4u;  // an odd number of float4s: lane-per-row reads hit distinct banks
+    const uint32_t cap = cluster_keys_cap(window);
+    float* ks = sm;
+    float* vs = ks + static_cast<size_t>(cap) * pitch;
+    float* qs = vs + static_cast<size_t>(cap) * pitch;
+    float* slots = qs + hd;  // the leader's receive the partials
+    const uint32_t rank = cluster_cta_rank();
+    const uint32_t h = blockIdx.y, qpk = nq / nkv, kh = h / qpk, kvd = nkv * hd;
+    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31u, half = hd / 2u, hd4 = hd / 4u;
+    const uint64_t pos = __ldcg(reinterpret_cast<const unsigned long long*>(&io->pos));
+    const uint64_t start = pos + 1 > window ? pos + 1 - window : 0;
+    const uint32_t nctx = static_cast<uint32_t>(pos - start + 1);
+    const uint32_t per = (nctx + kClusterCtas - 1u) / kClusterCtas;  // <= cap
+    const uint32_t jb = rank * per < nctx ? rank * per : nctx;
+    const uint32_t je = jb + per < nctx ? jb + per : nctx;
+    const uint32_t nk = je - jb;
+    const uint32_t jcur = nctx - 1;  // the current position's key
+    const bool has_cur = jcur >= jb && jcur < je;
+    const size_t cur_slot = static_cast<size_t>(pos % window) * kvd + static_cast<size_t>(kh) * hd;
+    for (uint32_t i = t; i < nk * hd4; i += kAttnThreads) {
+        const uint32_t j = i / hd4, c = i - j * hd4;
+        if (jb + j == jcur) continue;
+        const size_t off = static_cast<size_t>((start + jb + j) % window) * kvd + static_cast<size_t>(kh) * hd + 4u * c;
+        cp_async16(ks + j * pitch + 4u * c, kcache + off);
+        cp_async16(vs + j * pitch + 4u * c, vcache + off);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    dep_wait();
+    dep_launch();
+    const float* q = qkv + static_cast<size_t>(h) * hd;
+    const float* k = qkv + static_cast<size_t>(nq) * hd + static_cast<size_t>(kh) * hd;
+    const float* v = qkv + static_cast<size_t>(nq) * hd + kvd + static_cast<size_t>(kh) * hd;
+    for (uint32_t i = t; i < half; i += kAttnThreads) {
+        const float freq = powf(theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+        const float a = static_cast<float>(pos) * freq;
+        const float c = cosf(a), sn = sinf(a);
+        const float x0 = q[i], y0 = q[i + half];
+        qs[i] = x0 * c - y0 * sn;
+        qs[i + half] = x0 * sn + y0 * c;
+        if (has_cur) {
+            const float kx = k[i], ky = k[i + half];
+            const float k0 = kx * c - ky * sn, k1 = kx * sn + ky * c;
+            const float v0 = v[i], v1 = v[i + half];
+            float* kr = ks + (jcur - jb) * pitch;
+            float* vr = vs + (jcur - jb) * pitch;
+            kr[i] = k0;
+            kr[i + half] = k1;
+            vr[i] = v0;
+            vr[i + half] = v1;
+            if (h % qpk == 0) {
+                kcache[cur_slot + i] = k0;
+                kcache[cur_slot + i + half] = k1;
+                vcache[cur_slot + i] = v0;
+                vcache[cur_slot + i + half] = v1;
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    constexpr uint32_t kDims = kMaxClusterHd / 32u;  // value dimensions per lane
+    float m = -INFINITY, l = 0.f;
+    float acc[kDims];
+#pragma unroll
+    for (uint32_t k2 = 0; k2 < kDims; ++k2) acc[k2] = 0.f;
+    const float4* q4p = reinterpret_cast<const float4*>(qs);
+    const uint32_t nchunks = (nk + 31u) / 32u;
+    for (uint32_t c = warp; c < nchunks; c += kAttnWarps) {
+        const uint32_t j = c * 32u + lane;
+        const bool valid = j < nk;
+        double dot = 0.0;
+        if (valid) {
+            const float4* kr = reinterpret_cast<const float4*>(ks + j * pitch);
+            for (uint32_t cc = 0; cc < hd4; ++cc) {
+                const float4 q4 = q4p[cc], k4 = kr[cc];
+                dot += static_cast<double>(q4.x) * k4.x;
+                dot += static_cast<double>(q4.y) * k4.y;
+                dot += static_cast<double>(q4.z) * k4.z;
+                dot += static_cast<double>(q4.w) * k4.w;
+            }
+        }
+        const float sc = valid ? static_cast<float>(dot) * inv_sqrt_hd : -INFINITY;
+        float mc = sc;
+        for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xFFFFFFFFu, mc, o));
+        const float mn = fmaxf(m, mc);  // finite: the chunk holds a key
+        const float scale = expf(m - mn);
+        const float e = valid ? expf(sc - mn) : 0.f;
+        float es = e;
+        for (int o = 16; o > 0; o >>= 1) es += __shfl_xor_sync(0xFFFFFFFFu, es, o);
+        l = l * scale + es;
+#pragma unroll
+        for (uint32_t k2 = 0; k2 < kDims; ++k2) acc[k2] *= scale;
+        const uint32_t kn = nk - c * 32u < 32u ? nk - c * 32u : 32u;
+        for (uint32_t jj = 0; jj < kn; ++jj) {
+            const float ej = __shfl_sync(0xFFFFFFFFu, e, jj);
+            const float* vr = vs + (c * 32u + jj) * pitch;
+#pragma unroll
+            for (uint32_t k2 = 0; k2 < kDims; ++k2) {
+                const uint32_t d = lane + 32u * k2;
+                if (d < hd) acc[k2] = fmaf(ej, vr[d], acc[k2]);
+            }
+        }
+        m = mn;
+    }
+    // this warp's partial into slot (rank, warp) of the leader
+    const uint32_t base = cluster_addr(slots + static_cast<size_t>(rank * kAttnWarps + warp) * (hd + 2u), 0);
+#pragma unroll
+    for (uint32_t k2 = 0; k2 < kDims; ++k2) {
+        const uint32_t d = lane + 32u * k2;
+        if (d < hd) st_cluster(base + 4u * d, acc[k2]);
+    }
+    if (lane == 0) {
+        st_cluster(base + 4u * hd, m);
+        st_cluster(base + 4u * (hd + 1u), l);
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (rank != 0) return;
+    if (t < kClusterParts) {
+        float M = -INFINITY;
+        for (uint32_t i = 0; i < kClusterParts; ++i) M = fmaxf(M, slots[i * (hd + 2u) + hd]);
+        wsl[t] = expf(slots[t * (hd + 2u) + hd] - M);
+    }
+    __syncthreads();
+    float L = 0.f;
+    for (uint32_t i = 0; i < kClusterParts; ++i) L = fmaf(slots[i * (hd + 2u) + hd + 1u], wsl[i], L);
+    const float inv = 1.0f / L;
+    for (uint32_t d = t; d < hd; d += kAttnThreads) {
+        float o = 0.f;
+        for (uint32_t i = 0; i < kClusterParts; ++i) o = fmaf(slots[i * (hd + 2u) + d], wsl[i], o);
+        att[static_cast<size_t>(h) * hd + d] = o * inv;
+    }
 }
 
 // gate = silu(gate) * up with gu = [gate | up] (src/kernels.cpp:88-91), then
@@ -382,9 +591,23 @@ uint32_t attention_splits(uint32_t window) { return (window + kKeys - 1) / kKeys
 cudaError_t launch_attention(const float* qkv, float* kcache, float* vcache, float* att, float* part,
                              uint32_t* counter, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
                              uint32_t window, float theta, float inv_sqrt_hd, cudaStream_t stream, bool pdl) {
+    // NEDO_GPU_ATTENTION=split keeps every window on the split kernel (for comparisons)
+    static const bool split_only = [] {
+        const char* e = getenv("NEDO_GPU_ATTENTION");
+        return e != nullptr && strcmp(e, "split") == 0;
+    }();
+    const size_t csmem = attention_cluster_smem_floats(hd, window) * sizeof(float);
+    if (!split_only && hd <= kMaxClusterHd && csmem <= 200u * 1024u) {
+        // one cluster of kClusterCtas CTAs per query head
+        cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(csmem));
+        if (e != cudaSuccess) return e;
+        return launch(attention_cluster_kernel, dim3(kClusterCtas, nq), dim3(kAttnThreads), csmem, stream, pdl, qkv,
+                      kcache, vcache, att, io, nq, nkv, hd, window, theta, inv_sqrt_hd);
+    }
     const uint32_t ns = attention_splits(window);
-    // q, current k and v, the warps' value sums, the split weights
-    const size_t smem = ((3u + kAttnWarps) * static_cast<size_t>(hd) + ns) * sizeof(float);
+    const size_t smem = attention_smem_floats(hd) * sizeof(float);
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
     if (smem > 48u * 1024u) {
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));

@@ -761,6 +761,32 @@ __device__ __forceinline__ void item_dot(const uint8_t* r0, const uint8_t* r1, s
     }
 }
 
+// The producer's L2 prefetch of the KV-cache rows the next attention step reads
+// (XPrologue kcache): cached positions [start, pos) of the window, ring slots
+// (start + j) % window, this CTA's share of them in at most two contiguous runs.
+// The attention kernel's own copies of these rows, issued before its dependency
+// wait, then hit L2.
+__device__ __forceinline__ void prefetch_kv_rows(const XPrologue& pro) {
+    const uint64_t pos = __ldcg(reinterpret_cast<const unsigned long long*>(&pro.io->pos));
+    const uint64_t start = pos + 1 > pro.window ? pos + 1 - pro.window : 0;
+    const uint64_t n = pos - start;  // cached rows (the current one comes from this kernel's output)
+    const uint64_t j0 = n * blockIdx.x / gridDim.x, j1 = n * (blockIdx.x + 1) / gridDim.x;
+    uint64_t j = j0;
+    while (j < j1) {
+        const uint64_t slot = (start + j) % pro.window;
+        const uint64_t run = j1 - j < pro.window - slot ? j1 - j : pro.window - slot;
+        const uint64_t off = slot * pro.row_bytes;
+        const uint32_t bytes = static_cast<uint32_t>(run * pro.row_bytes);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const uint8_t*>(pro.kcache) + off),
+                     "r"(bytes)
+                     : "memory");
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const uint8_t*>(pro.vcache) + off),
+                     "r"(bytes)
+                     : "memory");
+        j += run;
+    }
+}
+
 template <uint32_t TYPE, uint32_t UP, uint32_t R>
 __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ CUtensorMap map, const ImmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -824,6 +850,7 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
             grid_launch_dependents();
         }
         if (!ok) *abort_flag = 1u;
+        if (a.pro.kcache != nullptr) prefetch_kv_rows(a.pro);
         // every issued copy lands before the CTA may exit
         for (uint32_t c = 0, k = 0; c < nchunk; ++c)
             for (uint32_t t = 0; t < my_tiles && k < issued; ++t, ++k)

@@ -129,8 +129,16 @@ struct XPrologue {
     float* x_out = nullptr;        // norm: x + delta (may be null)
     const float* up = nullptr;     // silu: the up half
     const float* route = nullptr;  // silu: MorphFFN flags [vocab][2] (null: no masking)
-    const DecodeIo* io = nullptr;  // silu with route: the token
+    const DecodeIo* io = nullptr;  // silu with route: the token; cache prefetch: the position
     uint32_t m_shared = 0, m_root = 0, m_suffix = 0;
+    // L2 prefetch of a layer's KV-cache rows for the attention step that follows
+    // (kcache non-null): the rows of the window's cached positions before io->pos,
+    // a ring of `window` rows of `row_bytes` (a multiple of 16) for keys and for
+    // values, shared out among the CTAs
+    const float* kcache = nullptr;
+    const float* vcache = nullptr;
+    uint32_t window = 0;
+    uint32_t row_bytes = 0;
 };
 cudaError_t launch_imma(const ImmaPlan& plan, const void* w, const float* x, float* y, uint64_t rows, uint64_t cols,
                         DeviceStatus* status, cudaStream_t stream, bool pdl, const PeerGather* gather = nullptr,

@@ -1202,7 +1202,7 @@ int dec_enqueue(nedo_gpu_decoder* d) {
     float* xalt = d->x2;
     const float* pending = nullptr;  // a residual not yet added to xcur
     auto norm_into = [&](bool fused, const void* nw, uint32_t nwt, uint32_t type, uint64_t rows, const void* w,
-                         float* y) -> int {
+                         float* y, const float* kc, const float* vc) -> int {
         if (fused) {
             XPrologue pro;
             pro.mode = kPrologueNorm;
@@ -1211,6 +1211,14 @@ int dec_enqueue(nedo_gpu_decoder* d) {
             pro.wtype = nwt == 0 ? 0u : 1u;
             pro.eps = c.rms_eps;
             pro.x_out = xalt;
+            if (kc != nullptr) {
+                // the q|k|v projection also brings this layer's cached keys and values into L2
+                pro.kcache = kc;
+                pro.vcache = vc;
+                pro.io = d->io;
+                pro.window = d->window;
+                pro.row_bytes = d->kvd * static_cast<uint32_t>(sizeof(float));
+            }
             if (int rc = matvec_fused(s, type, rows, c.dim, w, xcur, y, pro, st)) return rc;
             std::swap(xcur, xalt);
         } else {
@@ -1223,15 +1231,17 @@ int dec_enqueue(nedo_gpu_decoder* d) {
     };
     for (uint32_t li = 0; li < c.layers; ++li) {
         const DecLayer& L = d->layers[li];
-        if (int rc = norm_into(L.qkv_fused, L.an, L.an_type, L.qkv_type, d->qd + 2u * d->kvd, L.qkv, d->qkv)) return rc;
         float* kc = d->kcache + li * cache_layer;
         float* vc = d->vcache + li * cache_layer;
+        if (int rc = norm_into(L.qkv_fused, L.an, L.an_type, L.qkv_type, d->qd + 2u * d->kvd, L.qkv, d->qkv, kc, vc))
+            return rc;
         e = launch_attention(d->qkv, kc, vc, d->att, d->attn_part, d->attn_counter, d->io, c.heads, c.kv_heads, hd,
                              d->window, c.rope_theta, inv_sqrt_hd, st, pdl);
         if (e != cudaSuccess) return cuda_fail(e, "attention launch");
         if (int rc = dispatch_matvec(s, L.o_type, c.dim, d->qd, L.o, d->att, d->tmp, 1, nullptr, st, 1)) return rc;
         pending = d->tmp;
-        if (int rc = norm_into(L.gu_fused, L.fn, L.fn_type, L.gu_type, 2u * c.ffn, L.gu, d->gu)) return rc;
+        if (int rc = norm_into(L.gu_fused, L.fn, L.fn_type, L.gu_type, 2u * c.ffn, L.gu, d->gu, nullptr, nullptr))
+            return rc;
         // MorphFFN occupies the trailing morph_layers blocks (src/model.cpp:200)
         const bool morph = d->route != nullptr && li + c.morph_layers >= c.layers;
         if (L.down_fused) {
