@@ -10,8 +10,6 @@
 // with griddepcontrol.wait (programmatic dependent launch) before it reads
 // anything that predecessor wrote.
 #include <math.h>
-#include <stdlib.h>
-#include <string.h>
 
 #include "common.cuh"
 #include "launch.h"
@@ -36,17 +34,6 @@ __device__ T block_sum(T v, T* red) {
     T s = red[0];
     for (uint32_t i = 1; i < nw; ++i) s += red[i];
     return s;
-}
-
-__device__ float block_max(float v, float* red) {
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-    const uint32_t w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31u) == 0) red[w] = v;
-    __syncthreads();
-    float m = red[0];
-    for (uint32_t i = 1; i < nw; ++i) m = fmaxf(m, red[i]);
-    return m;
 }
 
 // x = embedding row io->token of w (src/kernels.cpp:170-176).
@@ -120,7 +107,10 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 //     copied into shared memory (cp.async, L2 only): the cache was written by
 //     earlier passes, which completed before the previous kernel of this pass
 //     passed its own dependency wait, and the position comes from `io`, which
-//     the previous pass's last kernel (or the host) wrote;
+//     the previous pass's last kernel (or the host) wrote.  The q|k|v
+//     projection before this kernel prefetches the same rows into L2, so the
+//     copies are L2 hits (copies still in flight delay this kernel's
+//     dependency wait: measured ~4.7 us for 6 MB from HBM, ~3.6 us from L2);
 //   * RoPE of q_h (every CTA of the head computes the same rotated vector);
 //   * the current position's key and value (the last key of the window) are
 //     rotated / copied from qkv by the CTA whose split holds that key; the
@@ -326,190 +316,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     if (t == 0) counter[h] = 0u;
 }
 
-// Attention as one cluster of kClusterCtas CTAs per query head, for windows
-// whose keys per CTA fit in shared memory.  CTA r of head h takes the keys
-// [r * per, (r + 1) * per) of the window, per = ceil(n / kClusterCtas); its
-// cached keys and values are copied into shared memory before the dependency
-// wait and the current position's key and value come from qkv, as in
-// attention_kernel.  Warp w runs an online softmax over the CTA's 32-key
-// chunks w, w + 4, ...: per chunk the scores (lane = key, the dot in double),
-// the running maximum m, the sum l and the value sums acc[d] (lanes =
-// dimensions), rescaled by exp(m_old - m).  Every warp's (acc, m, l) goes
-// into the cluster leader's shared memory (distributed shared-memory
-// stores); after one cluster barrier the leader adds the partials in (CTA,
-// warp) order -- out[d] = sum_i acc_i[d] w_i / sum_i l_i w_i, w_i = exp(m_i - M)
-// -- and writes the head's output: no global round trip, no counter.
-constexpr uint32_t kClusterCtas = 8;
-constexpr uint32_t kMaxClusterHd = 256;
-constexpr uint32_t kClusterParts = kClusterCtas * kAttnWarps;
-
-// Keys one CTA of the cluster kernel holds: ceil(window / kClusterCtas) rounded up to 32.
-__host__ __device__ constexpr uint32_t cluster_keys_cap(uint32_t window) {
-    return ((window + kClusterCtas - 1u) / kClusterCtas + 31u) / 32u * 32u;
-}
-
-// Shared floats of attention_cluster_kernel: keys and values [cap][hd + 4], q [hd],
-// the partial slots [kClusterParts][hd + 2].
-__host__ __device__ constexpr size_t attention_cluster_smem_floats(uint32_t hd, uint32_t window) {
-    return 2u * static_cast<size_t>(cluster_keys_cap(window)) * (hd + 4u) + hd +
-           static_cast<size_t>(kClusterParts) * (hd + 2u);
-}
-
-__device__ __forceinline__ uint32_t cluster_cta_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// shared::cluster address of `p` (this CTA's shared memory) in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr(p)), "r"(rank));
-    return d;
-}
-
-__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kAttnThreads)
-    attention_cluster_kernel(const float* __restrict__ qkv, float* __restrict__ kcache, float* __restrict__ vcache,
-                             float* __restrict__ att, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
-                             uint32_t window, float theta, float inv_sqrt_hd) {
-    extern __shared__ __align__(16) float sm[];
-    __shared__ float wsl[kClusterParts];
-    const uint32_t pitch = hd + 4u;  // an odd number of float4s: lane-per-row reads hit distinct banks
-    const uint32_t cap = cluster_keys_cap(window);
-    float* ks = sm;
-    float* vs = ks + static_cast<size_t>(cap) * pitch;
-    float* qs = vs + static_cast<size_t>(cap) * pitch;
-    float* slots = qs + hd;  // the leader's receive the partials
-    const uint32_t rank = cluster_cta_rank();
-    const uint32_t h = blockIdx.y, qpk = nq / nkv, kh = h / qpk, kvd = nkv * hd;
-    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31u, half = hd / 2u, hd4 = hd / 4u;
-    const uint64_t pos = __ldcg(reinterpret_cast<const unsigned long long*>(&io->pos));
-    const uint64_t start = pos + 1 > window ? pos + 1 - window : 0;
-    const uint32_t nctx = static_cast<uint32_t>(pos - start + 1);
-    const uint32_t per = (nctx + kClusterCtas - 1u) / kClusterCtas;  // <= cap
-    const uint32_t jb = rank * per < nctx ? rank * per : nctx;
-    const uint32_t je = jb + per < nctx ? jb + per : nctx;
-    const uint32_t nk = je - jb;
-    const uint32_t jcur = nctx - 1;  // the current position's key
-    const bool has_cur = jcur >= jb && jcur < je;
-    const size_t cur_slot = static_cast<size_t>(pos % window) * kvd + static_cast<size_t>(kh) * hd;
-    for (uint32_t i = t; i < nk * hd4; i += kAttnThreads) {
-        const uint32_t j = i / hd4, c = i - j * hd4;
-        if (jb + j == jcur) continue;
-        const size_t off = static_cast<size_t>((start + jb + j) % window) * kvd + static_cast<size_t>(kh) * hd + 4u * c;
-        cp_async16(ks + j * pitch + 4u * c, kcache + off);
-        cp_async16(vs + j * pitch + 4u * c, vcache + off);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    dep_wait();
-    dep_launch();
-    const float* q = qkv + static_cast<size_t>(h) * hd;
-    const float* k = qkv + static_cast<size_t>(nq) * hd + static_cast<size_t>(kh) * hd;
-    const float* v = qkv + static_cast<size_t>(nq) * hd + kvd + static_cast<size_t>(kh) * hd;
-    for (uint32_t i = t; i < half; i += kAttnThreads) {
-        const float freq = powf(theta, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
-        const float a = static_cast<float>(pos) * freq;
-        const float c = cosf(a), sn = sinf(a);
-        const float x0 = q[i], y0 = q[i + half];
-        qs[i] = x0 * c - y0 * sn;
-        qs[i + half] = x0 * sn + y0 * c;
-        if (has_cur) {
-            const float kx = k[i], ky = k[i + half];
-            const float k0 = kx * c - ky * sn, k1 = kx * sn + ky * c;
-            const float v0 = v[i], v1 = v[i + half];
-            float* kr = ks + (jcur - jb) * pitch;
-            float* vr = vs + (jcur - jb) * pitch;
-            kr[i] = k0;
-            kr[i + half] = k1;
-            vr[i] = v0;
-            vr[i + half] = v1;
-            if (h % qpk == 0) {
-                kcache[cur_slot + i] = k0;
-                kcache[cur_slot + i + half] = k1;
-                vcache[cur_slot + i] = v0;
-                vcache[cur_slot + i + half] = v1;
-            }
-        }
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    constexpr uint32_t kDims = kMaxClusterHd / 32u;  // value dimensions per lane
-    float m = -INFINITY, l = 0.f;
-    float acc[kDims];
-#pragma unroll
-    for (uint32_t k2 = 0; k2 < kDims; ++k2) acc[k2] = 0.f;
-    const float4* q4p = reinterpret_cast<const float4*>(qs);
-    const uint32_t nchunks = (nk + 31u) / 32u;
-    for (uint32_t c = warp; c < nchunks; c += kAttnWarps) {
-        const uint32_t j = c * 32u + lane;
-        const bool valid = j < nk;
-        double dot = 0.0;
-        if (valid) {
-            const float4* kr = reinterpret_cast<const float4*>(ks + j * pitch);
-            for (uint32_t cc = 0; cc < hd4; ++cc) {
-                const float4 q4 = q4p[cc], k4 = kr[cc];
-                dot += static_cast<double>(q4.x) * k4.x;
-                dot += static_cast<double>(q4.y) * k4.y;
-                dot += static_cast<double>(q4.z) * k4.z;
-                dot += static_cast<double>(q4.w) * k4.w;
-            }
-        }
-        const float sc = valid ? static_cast<float>(dot) * inv_sqrt_hd : -INFINITY;
-        float mc = sc;
-        for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xFFFFFFFFu, mc, o));
-        const float mn = fmaxf(m, mc);  // finite: the chunk holds a key
-        const float scale = expf(m - mn);
-        const float e = valid ? expf(sc - mn) : 0.f;
-        float es = e;
-        for (int o = 16; o > 0; o >>= 1) es += __shfl_xor_sync(0xFFFFFFFFu, es, o);
-        l = l * scale + es;
-#pragma unroll
-        for (uint32_t k2 = 0; k2 < kDims; ++k2) acc[k2] *= scale;
-        const uint32_t kn = nk - c * 32u < 32u ? nk - c * 32u : 32u;
-        for (uint32_t jj = 0; jj < kn; ++jj) {
-            const float ej = __shfl_sync(0xFFFFFFFFu, e, jj);
-            const float* vr = vs + (c * 32u + jj) * pitch;
-#pragma unroll
-            for (uint32_t k2 = 0; k2 < kDims; ++k2) {
-                const uint32_t d = lane + 32u * k2;
-                if (d < hd) acc[k2] = fmaf(ej, vr[d], acc[k2]);
-            }
-        }
-        m = mn;
-    }
-    // this warp's partial into slot (rank, warp) of the leader
-    const uint32_t base = cluster_addr(slots + static_cast<size_t>(rank * kAttnWarps + warp) * (hd + 2u), 0);
-#pragma unroll
-    for (uint32_t k2 = 0; k2 < kDims; ++k2) {
-        const uint32_t d = lane + 32u * k2;
-        if (d < hd) st_cluster(base + 4u * d, acc[k2]);
-    }
-    if (lane == 0) {
-        st_cluster(base + 4u * hd, m);
-        st_cluster(base + 4u * (hd + 1u), l);
-    }
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    if (rank != 0) return;
-    if (t < kClusterParts) {
-        float M = -INFINITY;
-        for (uint32_t i = 0; i < kClusterParts; ++i) M = fmaxf(M, slots[i * (hd + 2u) + hd]);
-        wsl[t] = expf(slots[t * (hd + 2u) + hd] - M);
-    }
-    __syncthreads();
-    float L = 0.f;
-    for (uint32_t i = 0; i < kClusterParts; ++i) L = fmaf(slots[i * (hd + 2u) + hd + 1u], wsl[i], L);
-    const float inv = 1.0f / L;
-    for (uint32_t d = t; d < hd; d += kAttnThreads) {
-        float o = 0.f;
-        for (uint32_t i = 0; i < kClusterParts; ++i) o = fmaf(slots[i * (hd + 2u) + d], wsl[i], o);
-        att[static_cast<size_t>(h) * hd + d] = o * inv;
-    }
-}
-
 // gate = silu(gate) * up with gu = [gate | up] (src/kernels.cpp:88-91), then
 // the MorphFFN masking of the trailing layers (src/model.cpp:196-209): the
 // root and suffix neuron ranges are zeroed when the token's routing flags are
@@ -591,20 +397,6 @@ uint32_t attention_splits(uint32_t window) { return (window + kKeys - 1) / kKeys
 cudaError_t launch_attention(const float* qkv, float* kcache, float* vcache, float* att, float* part,
                              uint32_t* counter, const DecodeIo* io, uint32_t nq, uint32_t nkv, uint32_t hd,
                              uint32_t window, float theta, float inv_sqrt_hd, cudaStream_t stream, bool pdl) {
-    // NEDO_GPU_ATTENTION=split keeps every window on the split kernel (for comparisons)
-    static const bool split_only = [] {
-        const char* e = getenv("NEDO_GPU_ATTENTION");
-        return e != nullptr && strcmp(e, "split") == 0;
-    }();
-    const size_t csmem = attention_cluster_smem_floats(hd, window) * sizeof(float);
-    if (!split_only && hd <= kMaxClusterHd && csmem <= 200u * 1024u) {
-        // one cluster of kClusterCtas CTAs per query head
-        cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(csmem));
-        if (e != cudaSuccess) return e;
-        return launch(attention_cluster_kernel, dim3(kClusterCtas, nq), dim3(kAttnThreads), csmem, stream, pdl, qkv,
-                      kcache, vcache, att, io, nq, nkv, hd, window, theta, inv_sqrt_hd);
-    }
     const uint32_t ns = attention_splits(window);
     const size_t smem = attention_smem_floats(hd) * sizeof(float);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;

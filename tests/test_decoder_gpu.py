@@ -196,34 +196,3 @@ def test_cpp_dropin_decoder_matches_reference(cuda, tmp_path, name):
     assert all(int(picks[k]) == int(np.argmax(lg[k])) for k in range(passes))
     assert gen == ids
 
-
-SPLIT_CHILD = r"""
-import os, sys, tempfile
-sys.path[:0] = [sys.argv[1] + "/oracle", sys.argv[1] + "/nedo.cpp_b200", sys.argv[1] + "/tests",
-                sys.argv[1] + "/tests/golden"]
-import torch
-import make_decode_golden as M
-import test_decoder_gpu as T
-from nedo_gpu import gguf as G
-from nedo_gpu.decoder import Decoder
-with tempfile.TemporaryDirectory() as d:
-    for name, (kw, prompt, max_new) in M.MODELS.items():
-        p = os.path.join(d, name + ".gguf")
-        G.synthetic_model(p, **kw)
-        g = G.GgufFile(p)
-        dec = Decoder.from_gguf(g)
-        model = (name, g, dec, prompt, max_new)
-        T.test_teacher_forced_logits_match_reference(model)
-        T.test_device_generation_matches_reference_ids(model)
-        dec.close()
-print("ok")
-"""
-
-
-def test_split_attention_kernel_matches_reference(cuda):
-    # windows too long for the cluster kernel run the split kernel with the
-    # last-arriver combine; NEDO_GPU_ATTENTION=split runs it on every model
-    env = dict(os.environ, NEDO_GPU_ATTENTION="split")
-    r = subprocess.run([sys.executable, "-c", SPLIT_CHILD, ROOT], capture_output=True, text=True, timeout=900,
-                       env=env)
-    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), (r.stdout[-2000:], r.stderr[-4000:])
