@@ -1041,27 +1041,39 @@ __global__ void __maxnreg__(96) gemv_imma_slice_kernel(const __grid_constant__ C
 }
 
 // ---------------------------------------------------------------------------
-// Multi-vector resident slice (2 to 16 token vectors per launch, whole rows in
+// Multi-vector resident slice (2 to 32 token vectors per launch, whole rows in
 // one column group).  The grid is G token groups of C CTAs: group k computes
 // the vectors [k * NT, k * NT + NT) over every tile, its C CTAs splitting the
-// tiles evenly (at most R each).  A CTA keeps its tiles resident as the
-// one-vector slice does and builds the x tables of its own NT vectors only, so
-// the table work per CTA shrinks as G grows; each weight tile is read from HBM
-// by one group and from L2 by the others.
+// tiles evenly.  A CTA keeps its tiles resident as the one-vector slice does
+// and builds the x tables of its own NT vectors only, so the table work per
+// CTA shrinks as G grows; each weight tile is read from HBM by one group and
+// from L2 by the others.
 //
-// Compute.  Warp w takes sub-segments w, w + W, ... (kMultiSub block pairs
-// each) of all the CTA's tiles for all NT vectors: per block pair and tile the
-// A fragments are loaded once and applied to every vector's B fragments, and
-// the sums stay in registers over the warp's sub-segments.  Once every warp is
-// done, each warp's row sums go into the tables' memory (no longer read) and
-// each (tile, vector) row is added over the warps in warp order, so the result
+// Compute.  The CTA's tiles are taken R at a time (the sums of R tiles x NT
+// vectors stay in registers); for each group of R tiles, warp w takes
+// sub-segments w, w + W, ... (kMultiSub block pairs each) for all NT vectors:
+// per block pair and tile the A fragments are loaded once and applied to
+// every vector's B fragments.  Each warp's row sums of the group go to its
+// own slots [warp][tile][vector][16]; once every warp is done, each
+// (tile, vector) row is added over the warps in warp order, so the result
 // depends only on the shape.
 constexpr uint32_t kMultiSub = 2;
+constexpr uint64_t kMultiCtaWeightBytes = 110u * 1024u;
 
-// Bytes of the tables / row-sums region of the multi-vector kernel.
-__host__ __device__ constexpr uint64_t multi_region_bytes(uint64_t nt, uint64_t pairs, uint64_t warps, uint64_t r) {
-    return nt * pairs * kPairTableBytes > warps * r * nt * 16u * 4u ? nt * pairs * kPairTableBytes
-                                                                    : warps * r * nt * 16u * 4u;
+// Bytes of the multi-vector kernel's tables (NT vectors) and row-sum slots
+// (`warps` x `tiles` x NT x 16 floats).  With at most R tiles per CTA (one
+// register group) the sums are written after the last table read and share
+// the tables' memory.
+__host__ __device__ constexpr uint64_t multi_table_bytes(uint64_t nt, uint64_t pairs) { return nt * pairs * kPairTableBytes; }
+__host__ __device__ constexpr uint64_t multi_sums_bytes(uint64_t nt, uint64_t warps, uint64_t tiles) {
+    return warps * tiles * nt * 16u * 4u;
+}
+__host__ __device__ constexpr uint64_t multi_region_bytes(uint64_t nt, uint64_t pairs, uint64_t warps, uint64_t tiles,
+                                                          uint64_t r) {
+    return tiles <= r ? (multi_table_bytes(nt, pairs) > multi_sums_bytes(nt, warps, tiles)
+                             ? multi_table_bytes(nt, pairs)
+                             : multi_sums_bytes(nt, warps, tiles))
+                      : multi_table_bytes(nt, pairs) + multi_sums_bytes(nt, warps, tiles);
 }
 
 // One sub-segment (`valid` <= kMultiSub block pairs) of nt <= R tiles (rows g /
@@ -1094,8 +1106,9 @@ __device__ __forceinline__ void multi_dot(const uint8_t* r0, const uint8_t* r1, 
 }
 
 // Registers: NT = 8 runs 12 consumer warps (13 warps, charged as 16) within 128,
-// fewer vectors 16 consumer warps (charged as 20) within 96.
-template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT>
+// fewer vectors 16 consumer warps (charged as 20) within 96.  GROUPS: a CTA may
+// hold more than R tiles (else one register group, its sums on the tables).
+template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT, bool GROUPS>
 __global__ void __maxnreg__(NT >= 8 ? 128 : 96) gemv_imma_multi_kernel(const __grid_constant__ CUtensorMap map,
                                                                       const ImmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1107,14 +1120,18 @@ __global__ void __maxnreg__(NT >= 8 ? 128 : 96) gemv_imma_multi_kernel(const __g
     const uint32_t grp = blockIdx.x / C, cta = blockIdx.x - grp * C;
     const uint32_t tile_begin = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * cta / C);
     const uint32_t tile_end = static_cast<uint32_t>(static_cast<uint64_t>(a.tiles) * (cta + 1) / C);
-    const uint32_t my_tiles = tile_end - tile_begin;  // 1 to R (planned)
+    const uint32_t my_tiles = tile_end - tile_begin;  // at least 1, at most slots / nchunk (planned)
     const uint32_t nchunk = (a.pairs_total + UP - 1u) / UP;
     const uint32_t nunits = my_tiles * nchunk;
+    const uint32_t tiles_cap = a.slots / nchunk;
     const size_t tstride = static_cast<size_t>(a.pairs_total) * kPairTableBytes;  // one vector's table
-    // [units: slots x unit_bytes, unit (t, c) at t * nchunk + c][tables: NT x tstride,
-    // later the warps' row sums][full: slots][x requested][abort flag]
+    // [units: slots x unit_bytes, unit (t, c) at t * nchunk + c][tables: NT x tstride]
+    // [row sums: W x tiles_cap x NT x 16 (on the tables when tiles_cap <= R)]
+    // [full: slots][x requested][abort flag]
+    constexpr bool one_group = !GROUPS;
     uint8_t* table = smem + static_cast<size_t>(a.slots) * a.unit_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(table + multi_region_bytes(NT, a.pairs_total, W, R));
+    float* part = reinterpret_cast<float*>(one_group ? table : table + multi_table_bytes(NT, a.pairs_total));
+    uint64_t* full = reinterpret_cast<uint64_t*>(table + multi_region_bytes(NT, a.pairs_total, W, tiles_cap, R));
     uint64_t* xbar = full + a.slots;
     volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(xbar + 1);
     const float* x = a.x + static_cast<size_t>(grp) * NT * a.ldx;
@@ -1199,45 +1216,51 @@ __global__ void __maxnreg__(NT >= 8 ? 128 : 96) gemv_imma_multi_kernel(const __g
 
     const uint32_t nsub = (a.pairs_total + kMultiSub - 1u) / kMultiSub;
     const size_t tstep = static_cast<size_t>(nchunk) * a.unit_bytes;  // unit (t + 1, c) - unit (t, c)
-    float acc0[R][NT], acc1[R][NT];
-#pragma unroll
-    for (uint32_t r = 0; r < R; ++r)
-#pragma unroll
-        for (uint32_t k = 0; k < NT; ++k) acc0[r][k] = acc1[r][k] = 0.f;
     bool ok = true;
-    for (uint32_t s = warp; s < nsub; s += W) {
-        const uint32_t p0 = s * kMultiSub, c = p0 / UP;  // kMultiSub divides UP: one chunk
-        if (ok && *abort_flag != 0u) ok = false;
-        for (uint32_t r = 0; r < my_tiles && ok; ++r)
-            if (!mbar_wait_bounded(&full[r * nchunk + c], 0u, a.status, 25u)) {
-                ok = false;
-                *abort_flag = 1u;
-            }
-        if (!ok) continue;
-        const uint8_t* unit = smem + static_cast<size_t>(c) * a.unit_bytes + static_cast<size_t>(p0 - c * UP) * pb;
-        const uint32_t left = a.pairs_total - p0;
-        multi_dot<TYPE, R, NT>(unit + off_a, unit + off_b, tstep, my_tiles,
-                               table + static_cast<size_t>(p0) * kPairTableBytes, tstride,
-                               left < kMultiSub ? left : kMultiSub, lane, even_mask, acc0, acc1);
-    }
-    named_barrier_sync(1, W * 32u);  // every warp is done with the tables
-    // this warp's row sums: part[warp][tile][vector][16 rows]; row r of a tile is
-    // acc0 (r < 8) or acc1 (r >= 8) of lane 4 (r mod 8) after folding the t-lanes
-    float* part = reinterpret_cast<float*>(table);
+    const uint32_t ngroups = GROUPS ? (my_tiles + R - 1u) / R : 1u;
+    for (uint32_t gi = 0; gi < ngroups; ++gi) {
+        const uint32_t t0 = gi * R;
+        const uint32_t nt = my_tiles - t0 < R ? my_tiles - t0 : R;
+        float acc0[R][NT], acc1[R][NT];
 #pragma unroll
-    for (uint32_t r = 0; r < R; ++r)
+        for (uint32_t r = 0; r < R; ++r)
 #pragma unroll
-        for (uint32_t k = 0; k < NT; ++k) {
-            float c0 = acc0[r][k], c1 = acc1[r][k];
-            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
-            c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
-            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
-            c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
-            const uint32_t rr = lane & 15u;
-            const float v0 = __shfl_sync(0xFFFFFFFFu, c0, 4u * (rr & 7u));
-            const float v1 = __shfl_sync(0xFFFFFFFFu, c1, 4u * (rr & 7u));
-            if (lane < 16) part[((static_cast<size_t>(warp) * R + r) * NT + k) * 16u + lane] = rr < 8 ? v0 : v1;
+            for (uint32_t k = 0; k < NT; ++k) acc0[r][k] = acc1[r][k] = 0.f;
+        for (uint32_t s = warp; s < nsub; s += W) {
+            const uint32_t p0 = s * kMultiSub, c = p0 / UP;  // kMultiSub divides UP: one chunk
+            if (ok && *abort_flag != 0u) ok = false;
+            for (uint32_t r = 0; r < nt && ok; ++r)
+                if (!mbar_wait_bounded(&full[(t0 + r) * nchunk + c], 0u, a.status, 25u)) {
+                    ok = false;
+                    *abort_flag = 1u;
+                }
+            if (!ok) continue;
+            const uint8_t* unit = smem + static_cast<size_t>(t0 * nchunk + c) * a.unit_bytes +
+                                  static_cast<size_t>(p0 - c * UP) * pb;
+            const uint32_t left = a.pairs_total - p0;
+            multi_dot<TYPE, R, NT>(unit + off_a, unit + off_b, tstep, nt,
+                                   table + static_cast<size_t>(p0) * kPairTableBytes, tstride,
+                                   left < kMultiSub ? left : kMultiSub, lane, even_mask, acc0, acc1);
         }
+        // this warp's row sums of the group: row r of a tile is acc0 (r < 8) or acc1
+        // (r >= 8) of lane 4 (r mod 8) after folding the t-lanes
+        if constexpr (one_group) named_barrier_sync(1, W * 32u);  // every warp is done with the tables
+#pragma unroll
+        for (uint32_t r = 0; r < R; ++r)
+#pragma unroll
+            for (uint32_t k = 0; k < NT; ++k) {
+                float c0 = acc0[r][k], c1 = acc1[r][k];
+                c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 1);
+                c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, 2);
+                c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 1);
+                c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, 2);
+                const uint32_t rr = lane & 15u;
+                const float v0 = __shfl_sync(0xFFFFFFFFu, c0, 4u * (rr & 7u));
+                const float v1 = __shfl_sync(0xFFFFFFFFu, c1, 4u * (rr & 7u));
+                if (lane < 16 && r < nt)
+                    part[((static_cast<size_t>(warp) * tiles_cap + t0 + r) * NT + k) * 16u + lane] = rr < 8 ? v0 : v1;
+            }
+    }
     named_barrier_sync(1, W * 32u);
     if (*abort_flag == 0u) {
         const uint32_t nw = nsub < W ? nsub : W;  // the warps that had sub-segments
@@ -1245,21 +1268,21 @@ __global__ void __maxnreg__(NT >= 8 ? 128 : 96) gemv_imma_multi_kernel(const __g
         for (uint32_t i = threadIdx.x; i < outs; i += W * 32u) {
             const uint32_t r = i / (NT * 16u), k = (i / 16u) % NT, row16 = i & 15u;
             float sum = 0.f;
-            for (uint32_t w = 0; w < nw; ++w) sum += part[((static_cast<size_t>(w) * R + r) * NT + k) * 16u + row16];
+            for (uint32_t w = 0; w < nw; ++w) sum += part[((static_cast<size_t>(w) * tiles_cap + r) * NT + k) * 16u + row16];
             const uint64_t row = static_cast<uint64_t>(tile_begin + r) * kTileRows + row16;
             if (row < a.rows) y[k * a.ldy + row] = sum;
         }
     }
 }
 
-template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT>
+template <uint32_t TYPE, uint32_t UP, uint32_t R, uint32_t NT, bool GROUPS>
 cudaError_t launch_multi_t(const ImmaPlan& plan, const CUtensorMap& map, const ImmaArgs& args, cudaStream_t stream,
                            bool pdl) {
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_imma_multi_kernel<TYPE, UP, R, NT>,
+        cudaError_t e = cudaFuncSetAttribute(gemv_imma_multi_kernel<TYPE, UP, R, NT, GROUPS>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
         configured[dev] = true;
@@ -1274,7 +1297,7 @@ cudaError_t launch_multi_t(const ImmaPlan& plan, const CUtensorMap& map, const I
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_imma_multi_kernel<TYPE, UP, R, NT>, map, args);
+    return cudaLaunchKernelEx(&cfg, gemv_imma_multi_kernel<TYPE, UP, R, NT, GROUPS>, map, args);
 }
 
 // Vectors per CTA: 2 (up to 8 tiles), 4 (up to 4) or 8 (up to 2): 32 row sums per lane.
@@ -1283,10 +1306,15 @@ cudaError_t launch_multi_p(const ImmaPlan& plan, const CUtensorMap& map, const I
                            bool pdl) {
     constexpr uint32_t UP = TYPE == kQ4_0 ? 32u : 16u;
     if (plan.seg_pairs != UP) return cudaErrorInvalidValue;
+    // more tiles per CTA than one register group of 16 / NT
+    const bool groups = plan.slots / ((plan.group_pairs + UP - 1u) / UP) > 16u / plan.tokens;
     switch (plan.tokens) {
-        case 2: return launch_multi_t<TYPE, UP, 8, 2>(plan, map, args, stream, pdl);
-        case 4: return launch_multi_t<TYPE, UP, 4, 4>(plan, map, args, stream, pdl);
-        case 8: return launch_multi_t<TYPE, UP, 2, 8>(plan, map, args, stream, pdl);
+        case 2: return groups ? launch_multi_t<TYPE, UP, 8, 2, true>(plan, map, args, stream, pdl)
+                              : launch_multi_t<TYPE, UP, 8, 2, false>(plan, map, args, stream, pdl);
+        case 4: return groups ? launch_multi_t<TYPE, UP, 4, 4, true>(plan, map, args, stream, pdl)
+                              : launch_multi_t<TYPE, UP, 4, 4, false>(plan, map, args, stream, pdl);
+        case 8: return groups ? launch_multi_t<TYPE, UP, 2, 8, true>(plan, map, args, stream, pdl)
+                              : launch_multi_t<TYPE, UP, 2, 8, false>(plan, map, args, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1555,23 +1583,39 @@ ImmaPlan plan_imma_multi(uint32_t type, uint64_t rows, uint64_t cols, int num_sm
     const uint64_t unit = kTileRows * box;
     const uint64_t nchunk = (pairs_total + up - 1) / up;
     const uint64_t tiles = (rows + kTileRows - 1) / kTileRows;
+    // Among the group sizes that fit: the most token groups whose CTAs hold at
+    // most kMultiCtaWeightBytes of weight each, else the smallest share of
+    // weight per CTA.  (Measured on 8-vector launches: the per-CTA weight
+    // share sets the time above ~100 KB -- 1536 x 4096 Q8_0 at 139 KB 8.9 us,
+    // 209 KB 12.4 us; 4096 x 1536 at 104 KB 6.7 us, 182 KB 10.7 us -- and below
+    // it more groups win: 1536 x 1536 with 4 groups of 2 vectors 4.95 us, 2
+    // groups of 4 5.3, 1 group of 8 6.1.)
+    uint64_t best_bytes = 0, best_groups = 0;
     const uint32_t per_group[3] = {2u, 4u, 8u};
     for (uint32_t nt : per_group) {
         if (vectors_per_group && nt != vectors_per_group) continue;
         if (tokens % nt) continue;
         const uint64_t groups = tokens / nt;
-        const uint64_t r_max = 16u / nt;  // tiles per CTA (the kernel's R)
+        const uint64_t r = 16u / nt;  // tiles per register group (the kernel's R)
         uint64_t ctas = static_cast<uint64_t>(num_sms) / groups;
         if (ctas == 0) continue;
         if (ctas > tiles) ctas = tiles;
         const uint64_t tpc = (tiles + ctas - 1) / ctas;
-        if (tpc > r_max) continue;
         const uint64_t warps = nt >= 8 ? 12u : kMaxWarps;
         // every (vector, block) of the tables in one pass of the consumer threads' registers
-        if (nt * 2u * pairs_total > warps * 4u * kLimbPasses) continue;
+        const uint64_t per_pass = warps * 4u;
+        if (nt * 2u * pairs_total > per_pass * kLimbPasses) continue;
         const uint64_t slots = tpc * nchunk;
-        const uint64_t smem = slots * unit + multi_region_bytes(nt, pairs_total, warps, r_max) + 8u * slots + 16u;
+        const uint64_t smem = slots * unit + multi_region_bytes(nt, pairs_total, warps, tpc, r) + 8u * slots + 16u;
         if (smem > static_cast<uint64_t>(max_smem_optin)) continue;
+        const uint64_t cta_bytes = tpc * kTileRows * rb;
+        if (p.ok) {
+            const bool small = cta_bytes <= kMultiCtaWeightBytes, best_small = best_bytes <= kMultiCtaWeightBytes;
+            const bool better = small ? (!best_small || groups > best_groups) : (!best_small && cta_bytes < best_bytes);
+            if (!better) continue;
+        }
+        best_bytes = cta_bytes;
+        best_groups = groups;
         p.type = type;
         p.wide = true;
         p.slice = false;
@@ -1590,13 +1634,12 @@ ImmaPlan plan_imma_multi(uint32_t type, uint64_t rows, uint64_t cols, int num_sm
         p.smem_bytes = static_cast<uint32_t>(smem);
         p.groups = 1;
         p.group_pairs = static_cast<uint32_t>(pairs_total);
-        p.tile_group = static_cast<uint32_t>(r_max);
+        p.tile_group = static_cast<uint32_t>(r);
         const uint64_t chunk_bytes = tpc * unit;
         uint64_t early = kEarlyBytes / chunk_bytes;
         if (early < 1) early = 1;
         p.early_chunks = static_cast<uint32_t>(early < nchunk ? early : nchunk);
         p.ok = true;
-        return p;
     }
     return p;
 }

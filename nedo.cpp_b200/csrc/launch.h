@@ -95,8 +95,9 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
                    const ImmaTuning* tune = nullptr, uint32_t tokens = 1);
 
 // The multi-vector resident slice for exactly `tokens` (>= 2) vectors in one
-// launch: token groups of 2, 4 or 8 vectors (the most groups that fit; only
-// `vectors_per_group` when it is non-zero), or !ok when none fits.
+// launch: token groups of 2, 4 or 8 vectors (the lowest estimated time among
+// those that fit; only `vectors_per_group` when it is non-zero), or !ok when
+// none fits.
 ImmaPlan plan_imma_multi(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
                          uint32_t tokens, uint32_t vectors_per_group = 0);
 

@@ -345,7 +345,7 @@ bool tc8_enabled() {
 }
 
 // Most token vectors one multi-vector launch takes.
-constexpr uint32_t kMultiMaxVectors = 16;
+constexpr uint32_t kMultiMaxVectors = 32;
 
 // NEDO_GPU_IMMA_MULTI: "0" keeps small batches on the ring kernel (for
 // comparisons), "2" / "4" / "8" fixes the vectors per token group (-1, 0 or
@@ -367,6 +367,14 @@ bool multi_applies(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols) 
     if ((type != kQ8_0 && type != kQ4_0) || multi_vectors_per_group() < 0) return false;
     const uint32_t g = multi_vectors_per_group();
     return plan_imma_multi(type, rows, cols, s->num_sms, s->max_smem, g > 0 ? g : 2u, g).ok;
+}
+
+// A batch of at most kMultiMaxVectors vectors that one multi-vector launch
+// takes whole: it runs there rather than on the fp16 GEMM (exact int8 block
+// dots, and one launch instead of the GEMM's conversion, GEMM and fold).
+bool multi_takes_whole_batch(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols, uint32_t batch) {
+    return batch >= 2 && batch <= kMultiMaxVectors && multi_applies(s, type, rows, cols) &&
+           plan_imma_multi(type, rows, cols, s->num_sms, s->max_smem, batch, multi_vectors_per_group()).ok;
 }
 
 // The launches of a batch on the multi-vector slice, in order: launches of up
@@ -421,7 +429,8 @@ int dispatch_matvec(DeviceState* s, uint32_t type, uint64_t rows, uint64_t cols,
         }
     }
     if (g_exact_batches.load() == 0 && batch >= tensor_core_min_batch(type) && cols >= kTensorCoreMinCols &&
-        amax == nullptr && aligned16(w) && aligned16(x) && gemm_tc_supported(type, rows, cols, batch)) {
+        amax == nullptr && aligned16(w) && aligned16(x) && gemm_tc_supported(type, rows, cols, batch) &&
+        !multi_takes_whole_batch(s, type, rows, cols, batch)) {
         // tokens as the N dimension of a tcgen05 GEMM (x rounded to fp16 once)
         const uint64_t n = static_cast<uint64_t>(batch) * cols;
         const uint32_t splits = gemm_tc_splits(rows, cols, batch, s->num_sms);
@@ -979,7 +988,8 @@ int nedo_gpu_plan_info(uint32_t type, uint64_t rows, uint64_t cols, uint32_t bat
     if (int rc = get_state(&s)) return rc;
     std::memset(out, 0, sizeof(uint32_t) * static_cast<size_t>(n));
     const bool tc = g_exact_batches.load() == 0 && batch >= tensor_core_min_batch(type) &&
-                    cols >= kTensorCoreMinCols && gemm_tc_supported(type, rows, cols, batch);
+                    cols >= kTensorCoreMinCols && gemm_tc_supported(type, rows, cols, batch) &&
+                    !multi_takes_whole_batch(s, type, rows, cols, batch);
     if (batch <= 1 && (type == kQ8_0 || type == kQ4_0) && tc8_enabled()) {
         Tc8Plan tp = plan_tc8(type, rows, cols, s->num_sms, s->max_smem);
         if (tp.ok) {

@@ -2,9 +2,10 @@
 C restatement of the reference (src/kernels.cpp:124-169): every output of every
 token vector within 1e-4 * sum|w*x|, and two runs bit-identical.
 
-A batch of 2 to 15 vectors (and, in exact mode, any batch) runs as launches of
-up to 16 vectors; each launch is split into token groups of 2, 4 or 8 vectors,
-one group of CTAs per group of vectors.  The shapes cover one to eight tiles
+A batch of 2 to 15 vectors, a batch of up to 32 that one launch takes whole,
+and in exact mode any batch, runs as launches of up to 32 vectors; each launch
+is split into token groups of 2, 4 or 8 vectors, one group of CTAs per group
+of vectors.  The shapes cover one to eight tiles
 per CTA, fewer tiles than CTAs, a last copy unit and a last work item that are
 partial, and rows the kernel does not take (the ring kernel then runs).  The
 batches cover a group-size remainder (odd batches end on the one-vector
@@ -64,10 +65,22 @@ def test_exact_mode_batches_of_16_and_more(lib, oracle, cuda, t):
         lib.set_exact_batches(prev)
 
 
+@pytest.mark.parametrize("t,rows,cols,batch", [(B.Q8_0, 1536, 1536, 16), (B.Q8_0, 1536, 1536, 32),
+                                                (B.Q4_0, 1536, 1536, 32), (B.Q8_0, 4096, 1536, 16),
+                                                (B.Q4_0, 4096, 1536, 16), (B.Q4_0, 1536, 4096, 16)])
+def test_whole_batch_in_one_launch(lib, oracle, cuda, t, rows, cols, batch):
+    # batches of 16 to 32 that one multi-vector launch takes stay off the fp16 GEMM
+    info = lib.plan_info(t, rows, cols, batch)
+    assert info["path"] == 4 and info["launches"] == 1, info
+    _check(lib, oracle, cuda, t, rows, cols, batch)
+
+
 def test_plan_reports_the_multi_vector_launch(lib, cuda):
-    # 1536x1536 Q8_0 at 8 vectors: 4 groups of 2 vectors over 37 CTAs each
+    # 1536x1536 Q8_0 at 8 vectors: 2 groups of 4 vectors over 74 CTAs each
     info = lib.plan_info(B.Q8_0, 1536, 1536, 8)
-    assert info["path"] == 4 and info["grid"] == 148 and info["warps"] == 16, info
+    assert info["path"] == 4 and info["grid"] == 148 and info["warps"] == 16 and info["launches"] == 1, info
+    # 11 vectors: launches of 10 and 1
+    assert lib.plan_info(B.Q8_0, 1536, 1536, 11)["launches"] == 2
 
 
 CHILD = r"""
