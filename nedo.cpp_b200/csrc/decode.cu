@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 //   * the last of the head's non-empty splits to finish (a self-resetting
 //     counter) adds them in split order, out[d] = sum_s acc_s[d] w_s /
 //     sum_s l_s w_s with w_s = exp(m_s - M), M the running maximum over rounds
-//     of 16 splits -- the same result whichever CTA is last.  Splits past the
+//     of 32 splits -- the same result whichever CTA is last.  Splits past the
 //     window's keys do nothing.
 constexpr uint32_t kKeys = 32;  // keys per split: one per lane
 constexpr uint32_t kAttnWarps = 4;
@@ -269,24 +269,29 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
             out[hd + 1] = ml[1];
         }
     }
-    // the last non-empty split of the head combines them
-    __threadfence();
+    // the last non-empty split of the head combines them.  The CTA barrier orders
+    // every thread's partial stores before thread 0's acquire-release add on the
+    // counter (cumulative at GPU scope); in the last CTA that add has acquired every
+    // other split's release, and the barrier after it passes that on to all threads.
     __syncthreads();
-    if (t == 0) last = atomicAdd(&counter[h], 1u) == nused - 1u ? 1u : 0u;
+    if (t == 0) {
+        uint32_t prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(counter + h) : "memory");
+        last = prev == nused - 1u ? 1u : 0u;
+    }
     __syncthreads();
     if (!last) return;
-    __threadfence();
-    // each thread's dimension: the splits' (m, l) and value sums, 16 splits per
+    // each thread's dimension: the splits' (m, l) and value sums, 32 splits per
     // round of loads, folded in split order with a running maximum (the same
     // maxima in every thread)
     const float* p = part + static_cast<size_t>(h) * gridDim.x * (hd + 2u);
     for (uint32_t d = t; d < hd; d += kAttnThreads) {
         float M = -INFINITY, L = 0.f, O = 0.f;
-        for (uint32_t i0 = 0; i0 < nused; i0 += 16u) {
-            const uint32_t nb = nused - i0 < 16u ? nused - i0 : 16u;
-            float mi[16], li[16], ai[16];
+        for (uint32_t i0 = 0; i0 < nused; i0 += 32u) {
+            const uint32_t nb = nused - i0 < 32u ? nused - i0 : 32u;
+            float mi[32], li[32], ai[32];
 #pragma unroll
-            for (uint32_t k2 = 0; k2 < 16; ++k2) {
+            for (uint32_t k2 = 0; k2 < 32; ++k2) {
                 if (k2 < nb) {
                     const float* pk = p + static_cast<size_t>(i0 + k2) * (hd + 2u);
                     mi[k2] = __ldcg(pk + hd);
@@ -296,13 +301,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
             }
             float mb = M;
 #pragma unroll
-            for (uint32_t k2 = 0; k2 < 16; ++k2)
+            for (uint32_t k2 = 0; k2 < 32; ++k2)
                 if (k2 < nb) mb = fmaxf(mb, mi[k2]);
             const float sc = expf(M - mb);  // 0 on the first round
             L *= sc;
             O *= sc;
 #pragma unroll
-            for (uint32_t k2 = 0; k2 < 16; ++k2) {
+            for (uint32_t k2 = 0; k2 < 32; ++k2) {
                 if (k2 < nb) {
                     const float w = expf(mi[k2] - mb);
                     L = fmaf(li[k2], w, L);

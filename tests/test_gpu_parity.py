@@ -181,15 +181,15 @@ def test_small_batch_int8_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
         assert_within_tol(y[b], ref[b], oracle.abs_dot(t, rows, cols, w, x[b]), what=f"batch item {b}")
 
 
-# Batches of >= 16 vectors run as one tcgen05 GEMM (fp16 x and d*q, fp32
-# accumulation): the same per-element tolerance against the reference's serial
-# matvecs.  Shapes cover ragged token tiles (tiles of 256), ragged row tiles
+# Batches of >= 16 vectors that one multi-vector int8 launch cannot take whole
+# run as one tcgen05 GEMM (fp16 x and d*q, fp32 accumulation): the same
+# per-element tolerance against the reference's serial matvecs.  Shapes cover ragged token tiles (tiles of 256), ragged row tiles
 # (128) and an odd number of 256-element weight chunks.
 @pytest.mark.parametrize("t", [B.Q8_0, B.Q4_0, B.F16])
 # The first three shapes have few 256-row tiles, so their K is split over several
 # CTAs (partial sums folded in split order); the last has enough tiles for one
 # CTA per tile.
-@pytest.mark.parametrize("rows,cols,batch", [(300, 2048, 16), (1000, 4096, 64), (129, 1280, 300), (19200, 2048, 16)])
+@pytest.mark.parametrize("rows,cols,batch", [(300, 2048, 40), (1000, 4096, 64), (129, 1280, 300), (19200, 2048, 16)])
 def test_batched_tensor_core_vs_reference(lib, cuda, oracle, t, rows, cols, batch):
     plan = lib.plan_info(t, rows, cols, batch)
     assert plan["path"] == 5, plan

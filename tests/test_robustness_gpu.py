@@ -91,31 +91,31 @@ def test_captured_batch_survives_buffer_growth(lib, cuda, oracle):
     t, rows, cols = B.Q8_0, 1000, 4096
     w = B.gen_weight(t, rows, cols, 93)
     wd = torch.from_numpy(w).cuda()
-    x16 = B.gen_x(cols, 93, batch=16)
+    x40 = B.gen_x(cols, 93, batch=40)
     x64 = B.gen_x(cols, 94, batch=64)
-    xd16, xd64 = torch.from_numpy(x16).cuda(), torch.from_numpy(x64).cuda()
-    y16 = torch.empty((16, rows), device="cuda")
+    xd40, xd64 = torch.from_numpy(x40).cuda(), torch.from_numpy(x64).cuda()
+    y40 = torch.empty((40, rows), device="cuda")
     y64 = torch.empty((64, rows), device="cuda")
-    assert lib.plan_info(t, rows, cols, 16)["path"] == 5
+    assert lib.plan_info(t, rows, cols, 40)["path"] == 5
     stream = torch.cuda.Stream()
-    lib.reserve(t, rows, cols, 16)  # sized outside capture
+    lib.reserve(t, rows, cols, 40)  # sized outside capture
     # one eager call first: per-process kernel set-up happens outside capture
-    lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd16.data_ptr(), y16.data_ptr(), 16, stream.cuda_stream)
+    lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd40.data_ptr(), y40.data_ptr(), 40, stream.cuda_stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd16.data_ptr(), y16.data_ptr(), 16, stream.cuda_stream)
+        lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd40.data_ptr(), y40.data_ptr(), 40, stream.cuda_stream)
     # a larger call grows the shared buffers (the captured ones are retired, not freed)
     lib.matvec_dev(t, rows, cols, wd.data_ptr(), xd64.data_ptr(), y64.data_ptr(), 64, _s(torch))
     torch.cuda.synchronize()
-    y16.zero_()
+    y40.zero_()
     graph.replay()
     torch.cuda.synchronize()
     lib.status()
-    ref16 = oracle.matvec_batch(t, rows, cols, w, x16)
-    got16 = y16.cpu().numpy()
-    for b in range(16):
-        assert_within_tol(got16[b], ref16[b], oracle.abs_dot(t, rows, cols, w, x16[b]), what=f"replayed token {b}")
+    ref40 = oracle.matvec_batch(t, rows, cols, w, x40)
+    got40 = y40.cpu().numpy()
+    for b in range(0, 40, 3):
+        assert_within_tol(got40[b], ref40[b], oracle.abs_dot(t, rows, cols, w, x40[b]), what=f"replayed token {b}")
     ref64 = oracle.matvec_batch(t, rows, cols, w, x64)
     got64 = y64.cpu().numpy()
     for b in range(0, 64, 7):
