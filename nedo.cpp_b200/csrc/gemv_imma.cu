@@ -1486,7 +1486,7 @@ ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int
             p.smem_bytes = static_cast<uint32_t>(smem);
             p.groups = 1;
             p.group_pairs = static_cast<uint32_t>(pairs_total);
-            p.tile_group = tiles_per_cta > 2 ? 5u : 2u;
+            p.tile_group = tiles_per_cta > 2 && (t.max_tile_group == 0 || t.max_tile_group >= 5u) ? 5u : 2u;
             // Copies issued before x is requested: x's loads queue behind this SM's
             // earlier weight copies, so only about as much as lands while the CTA
             // waits for the previous kernel (measured: ~150 KB) goes out first.

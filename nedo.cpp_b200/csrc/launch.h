@@ -89,6 +89,7 @@ struct ImmaTuning {
     uint32_t seg_pairs = 0;    // 8 or 16
     uint32_t smem_budget = 0;
     uint32_t table_budget = 0; // bytes of x table built at once (0 = default)
+    uint32_t max_tile_group = 0; // slice: at most this many tiles per work item (0 = up to 5)
 };
 
 ImmaPlan plan_imma(uint32_t type, uint64_t rows, uint64_t cols, int num_sms, int max_smem_optin,
