@@ -74,7 +74,9 @@ NEDO_GPU_API int nedo_gpu_set_pdl(int enable);
 
 /* Batched calls on the exact kernels only (process-wide, off by default).
  * By default a batch of 16 or more Q8_0/Q4_0 vectors (4 or more for F16) with
- * rows of at least 1024 elements runs one tcgen05 GEMM on fp16 operands: x
+ * rows of at least 1024 elements -- unless it is at most 32 vectors and one
+ * launch of the exact multi-vector int8 kernel takes it whole (small
+ * matrices) -- runs one tcgen05 GEMM on fp16 operands: x
  * and d*q are each rounded to fp16 once (relative error <= 2^-11 per
  * factor), products and sums are fp32.  Its worst-case error is therefore
  * about 2^-10 * sum_i |w_i x_i| per output, ten times the reference
@@ -82,10 +84,10 @@ NEDO_GPU_API int nedo_gpu_set_pdl(int enable);
  * of a row share one sign (e.g. a constant positive x against same-sign
  * weights); on independent inputs they cancel and the results stay within
  * the tolerance (tested at every benchmark shape).  When enabled, batches run
- * the int8 tensor-pipe kernel (exact integer block dots, x carried with 28
- * significant bits) or, for F16, one streaming pass per vector: within the
- * tolerance by bound, at the cost of one weight pass per 8 (int8) or 1 (F16)
- * vectors.  Returns the previous setting.  No reference counterpart. */
+ * the int8 tensor-pipe kernels (exact integer block dots, x carried with 28
+ * significant bits; up to 32 vectors per weight pass) or, for F16, one
+ * streaming pass per vector: within the tolerance by bound.  Returns the
+ * previous setting.  No reference counterpart. */
 NEDO_GPU_API int nedo_gpu_set_exact_batches(int enable);
 
 /* Message of the last failing call on this thread ("" if none). */
@@ -154,9 +156,12 @@ NEDO_GPU_API int nedo_gpu_cache_clear(void);
  * vectors: y_dev[b][r] = dot(row r, x_dev[b]), b < batch.  batch == 1 is the
  * decode path (src/model.cpp:217-259); batch > 1 replaces `batch` serial
  * calls over the same weight, which is how the reference processes a prompt
- * (src/model.cpp:262-266).  For rows of at least 1024 elements, from 16
- * vectors on (4 for F16 weights) the batch runs as one tensor-core GEMM with x
- * and the dequantised weight rounded to fp16 (fp32 accumulation).  Those
+ * (src/model.cpp:262-266).  Q8_0/Q4_0 batches of 2 to 15 vectors, and of up
+ * to 32 that one launch takes whole, run the exact multi-vector int8 kernel
+ * (each weight tile read once per launch for all its vectors).  Otherwise,
+ * for rows of at least 1024 elements, from 16 vectors on (4 for F16 weights)
+ * the batch runs as one tensor-core GEMM with x and the dequantised weight
+ * rounded to fp16 (fp32 accumulation).  The GEMM calls
  * calls use two per-device buffers (an fp16 copy of x and, for few row tiles,
  * a split-K workspace), allocated by the first call that needs them and grown
  * by a larger one.  A grown-out buffer stays allocated until
